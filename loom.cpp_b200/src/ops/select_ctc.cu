@@ -1,0 +1,190 @@
+// select_ctc.cu -- short rows, one warp per row: batched argmax of short rows and greedy CTC (K3).
+//
+// CTC replaces ctc_greedy_decode (src/core/ctc_decode.cpp:7-31) and the per-frame
+// ggml_backend_tensor_get + scan of argmax_tensor_rows (src/core/lua_bridge.cpp:343-365):
+//   1. per frame: argmax of the raw logits (strict '>' scan rule, NaN in column 0 wins), optionally
+//      its log-softmax value;
+//   2. per utterance, once all its frames are done (an atomic frame count per utterance; the CTA
+//      that completes it does the rest, nothing waits): keep frame f when id[f] != id[f-1] (id[-1] =
+//      blank) and id[f] != blank, then a block scan compacts the kept ids and their frame indices.
+// Each persistent CTA owns a contiguous, equal share of the n_utt * n_frames frames.
+// Bound: HBM bandwidth (one read of the logits; the per-frame ids are 4 bytes per frame).
+#include <cstdint>
+
+#include "select_internal.h"
+#include "select_rows.cuh"
+
+namespace loom_select {
+
+namespace {
+
+constexpr int kRowWarps = 8;
+constexpr int kRowNT = kRowWarps * 32;
+
+// ----------------------------------------------------------------------------------------------
+// batched argmax of short rows
+
+template <int kDtype>
+__global__ void __launch_bounds__(kRowNT) rows_argmax_kernel(const unsigned char* base, int64_t rows, int64_t width,
+                                                             int64_t stride_bytes, int64_t lo, int32_t* out_ids) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t r = gw; r < rows; r += nw) {
+        const unsigned char* row = base + r * stride_bytes;
+        ArgBest best;
+        LseAcc lse;
+        warp_row_reduce<kDtype, false>(row, width, best, lse);
+        if (lane == 0) {
+            const float x0 = load_global_elem<kDtype>(row, 0);
+            out_ids[r] = static_cast<int32_t>(lo + ((x0 != x0) ? 0 : best.i));
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------------------------
+// CTC
+
+struct CtcShared {
+    int n_last;
+    int64_t last_utt[4];
+    int warp_tot[kRowWarps];
+    int carry;
+};
+
+// Compacts utterance u's kept frames. Called by the whole CTA.
+__device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const int32_t* frame_ids, int32_t* out_ids,
+                             int32_t* out_frames, int32_t* out_len, CtcShared* sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int32_t* ids = frame_ids + u * n_frames;
+    if (threadIdx.x == 0) sh->carry = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < n_frames; base += kRowNT) {
+        const int64_t f = base + threadIdx.x;
+        int32_t id = 0;
+        bool keep = false;
+        if (f < n_frames) {
+            id = __ldcg(ids + f);
+            const int32_t prev = f == 0 ? blank : __ldcg(ids + f - 1);
+            keep = id != prev && id != blank;
+        }
+        const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) sh->warp_tot[warp] = __popc(ballot);
+        __syncthreads();
+        int before = sh->carry;
+        for (int w = 0; w < warp; ++w) before += sh->warp_tot[w];
+        int total = 0;
+        for (int w = 0; w < kRowWarps; ++w) total += sh->warp_tot[w];
+        if (keep) {
+            const int pos = before + __popc(ballot & ((1u << lane) - 1u));
+            out_ids[u * n_frames + pos] = id;
+            out_frames[u * n_frames + pos] = static_cast<int32_t>(f);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) sh->carry += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out_len[u] = sh->carry;
+    __syncthreads();
+}
+
+template <int kDtype, bool kLogp>
+__global__ void __launch_bounds__(kRowNT) ctc_kernel(const unsigned char* logits, int64_t n_utt, int64_t n_frames,
+                                                     int64_t n_classes, int32_t blank, int32_t* frame_ids,
+                                                     float* frame_logp, int32_t* out_ids, int32_t* out_frames,
+                                                     int32_t* out_len, int* tickets) {
+    constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
+    __shared__ CtcShared sh;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t total = n_utt * n_frames;
+    const int64_t f_lo = static_cast<int64_t>(blockIdx.x) * total / gridDim.x;
+    const int64_t f_hi = static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x;
+    const int64_t row_bytes = n_classes * kEsz;
+    for (int64_t f = f_lo + warp; f < f_hi; f += kRowWarps) {
+        const unsigned char* row = logits + f * row_bytes;
+        ArgBest best;
+        LseAcc lse;
+        warp_row_reduce<kDtype, kLogp>(row, n_classes, best, lse);
+        if (lane == 0) {
+            const float x0 = load_global_elem<kDtype>(row, 0);
+            const bool nan0 = x0 != x0;
+            frame_ids[f] = nan0 ? 0 : best.i;
+            if constexpr (kLogp) {
+                const double lp = nan0 ? static_cast<double>(x0)
+                                       : static_cast<double>(best.v) -
+                                             (static_cast<double>(lse.m) + log(static_cast<double>(lse.s)));
+                frame_logp[f] = static_cast<float>(lp);
+            }
+        }
+    }
+    // every frame of this CTA written -> count them into their utterances
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        sh.n_last = 0;
+        if (f_hi > f_lo) {
+            const int64_t u0 = f_lo / n_frames, u1 = (f_hi - 1) / n_frames;
+            for (int64_t u = u0; u <= u1; ++u) {
+                const int64_t a = u * n_frames > f_lo ? u * n_frames : f_lo;
+                const int64_t b = (u + 1) * n_frames < f_hi ? (u + 1) * n_frames : f_hi;
+                const int n = static_cast<int>(b - a);
+                const int prev = atomicAdd(&tickets[u], n);
+                if (prev + n == n_frames) sh.last_utt[sh.n_last++] = u;
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    const int n_last = sh.n_last;
+    for (int j = 0; j < n_last; ++j) {
+        const int64_t u = sh.last_utt[j];
+        ctc_collapse(u, n_frames, blank, frame_ids, out_ids, out_frames, out_len, &sh);
+        if (threadIdx.x == 0) tickets[u] = 0;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_rows_argmax(int dtype, const void* window_base, int64_t rows, int64_t width, int64_t row_stride,
+                               int64_t lo, int32_t* out_ids, int sms, cudaStream_t stream) {
+    const int64_t want = (rows + kRowWarps - 1) / kRowWarps;
+    const int64_t cap = static_cast<int64_t>(sms) * 8;
+    const int grid = static_cast<int>(want < cap ? want : cap);
+    const unsigned char* base = static_cast<const unsigned char*>(window_base);
+    if (dtype == LOOM_SELECT_BF16)
+        rows_argmax_kernel<LOOM_SELECT_BF16><<<grid, kRowNT, 0, stream>>>(base, rows, width, row_stride * 2, lo, out_ids);
+    else
+        rows_argmax_kernel<LOOM_SELECT_F32><<<grid, kRowNT, 0, stream>>>(base, rows, width, row_stride * 4, lo, out_ids);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ctc(int dtype, const void* logits, int64_t n_utt, int64_t n_frames, int64_t n_classes,
+                       int32_t blank, int32_t* out_ids, int32_t* out_frames, int32_t* out_len, int32_t* frame_ids,
+                       float* frame_logp, void* workspace, const WsLayout& l, int sms, cudaStream_t stream) {
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    int* tickets = reinterpret_cast<int*>(ws + l.tickets);
+    if (!frame_ids) frame_ids = reinterpret_cast<int32_t*>(ws + l.records);
+    const int64_t total = n_utt * n_frames;
+    // a CTA spans at most 4 utterances: enough CTAs that each holds <= 3 utterances' frames
+    int64_t grid = static_cast<int64_t>(sms) * 4;
+    const int64_t min_grid = (n_utt + 2) / 3 + 1;
+    if (grid < min_grid) grid = min_grid;
+    if (grid > total) grid = total;
+    const unsigned char* base = static_cast<const unsigned char*>(logits);
+    const bool lp = frame_logp != nullptr;
+#define LOOM_CTC_LAUNCH(DT, LP)                                                                                     \
+    ctc_kernel<DT, LP><<<static_cast<int>(grid), kRowNT, 0, stream>>>(base, n_utt, n_frames, n_classes, blank,      \
+                                                                       frame_ids, frame_logp, out_ids, out_frames, \
+                                                                       out_len, tickets)
+    if (dtype == LOOM_SELECT_BF16) {
+        if (lp) LOOM_CTC_LAUNCH(LOOM_SELECT_BF16, true);
+        else LOOM_CTC_LAUNCH(LOOM_SELECT_BF16, false);
+    } else {
+        if (lp) LOOM_CTC_LAUNCH(LOOM_SELECT_F32, true);
+        else LOOM_CTC_LAUNCH(LOOM_SELECT_F32, false);
+    }
+#undef LOOM_CTC_LAUNCH
+    return cudaGetLastError();
+}
+
+}  // namespace loom_select

@@ -1,0 +1,82 @@
+// select_internal.h -- host-side plumbing shared by the kernel files and the C-ABI (not installed).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "loom_select.h"
+
+namespace loom_select {
+
+// ---- workspace layout (every region 256-byte aligned) ----
+//   [0, 256)            status word (int32) of the device-side error report
+//   tickets             one int32 per row (or utterance), zero between calls
+//   records / frames    per-call scratch, fully written before it is read
+constexpr size_t kWsAlign = 256;
+inline size_t ws_round(size_t b) { return (b + kWsAlign - 1) / kWsAlign * kWsAlign; }
+
+constexpr int64_t kStreamSplitAlign = 64;
+constexpr int64_t kStreamMinRange = 8192;
+constexpr int kStreamMaxCtas = 1024;
+
+// A CTA's range splits at most two rows (its first and its last), so a streamed call needs at
+// most two partial-result records per CTA: slot 0 for the CTA's first row, slot 1 for its last.
+constexpr int64_t kStreamRecordSlots = 2 * kStreamMaxCtas;
+
+struct WsLayout {
+    size_t tickets = 0;
+    size_t records = 0;
+    size_t bytes = 0;
+};
+
+inline WsLayout ws_layout(int64_t n_tickets, size_t record_bytes, int64_t n_records) {
+    WsLayout l;
+    l.tickets = kWsAlign;
+    l.records = l.tickets + ws_round(static_cast<size_t>(n_tickets) * sizeof(int32_t));
+    l.bytes = l.records + ws_round(record_bytes * static_cast<size_t>(n_records));
+    return l;
+}
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count(int* status);
+
+// Launchers (validated arguments; return a cudaError_t from the launch).
+cudaError_t launch_argmax_stream(int dtype, const void* window_base, int64_t rows, int64_t width, int64_t row_stride,
+                                 int64_t lo, int32_t* out_ids, void* workspace, const WsLayout& l, int ctas,
+                                 cudaStream_t stream);
+
+cudaError_t launch_rows_argmax(int dtype, const void* window_base, int64_t rows, int64_t width, int64_t row_stride,
+                               int64_t lo, int32_t* out_ids, int sms, cudaStream_t stream);
+
+cudaError_t launch_ctc(int dtype, const void* logits, int64_t n_utt, int64_t n_frames, int64_t n_classes,
+                       int32_t blank, int32_t* out_ids, int32_t* out_frames, int32_t* out_len, int32_t* frame_ids,
+                       float* frame_logp, void* workspace, const WsLayout& l, int sms, cudaStream_t stream);
+
+struct SampleLaunch {
+    int dtype;
+    const void* logits;
+    int64_t rows, width, row_stride;
+    int64_t vocab_offset, vocab_limit;
+    const int32_t* history;
+    int32_t history_len;
+    const float* u;
+    float temperature, penalty, top_p;
+    int32_t top_k;
+    int32_t* out_ids;
+    float* out_prob;
+    float* out_logp;
+    int32_t* out_topk;
+    void* shard_out; // non-NULL: emit shard records instead of decisions
+};
+
+constexpr int kMaxHistory = 2048;
+
+size_t sample_record_bytes(int32_t top_k);
+cudaError_t launch_sample_stream(const SampleLaunch& a, void* workspace, const WsLayout& l, int ctas,
+                                 cudaStream_t stream);
+cudaError_t launch_shard_merge(const void* records, int32_t n_shards, int64_t rows, const float* u, int32_t top_k,
+                               float top_p, int32_t* out_ids, float* out_prob, float* out_logp, int32_t* out_topk,
+                               cudaStream_t stream);
+
+}  // namespace loom_select

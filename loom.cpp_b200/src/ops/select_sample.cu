@@ -1,0 +1,686 @@
+// select_sample.cu -- the fused sampling chain (K2) and the vocabulary-shard merge (K4).
+//
+// One pass over the logits: rows stream through shared memory (select_stream.cuh); per element the
+// only work is a compare of the raw logit against a threshold X. X is exact: it is the smallest x
+// whose tempered value x / T reaches the current k-th best tempered value, so every element below
+// it is strictly worse than k elements already kept. The few elements that pass are tempered with
+// an IEEE divide and appended to a shared-memory candidate buffer of 64-bit rank keys; when the
+// buffer fills, a radix select keeps the exact top-k and raises X.
+//
+// The repetition penalty touches only the history ids. They are marked in a per-stage bitmap: the
+// stream skips them and they are inserted separately with their penalised, tempered value, which
+// keeps the per-element path free of the penalty.
+//
+// The first stage of every row segment seeds X from the stage itself: each warp sorts its lanes'
+// maxima, and the smallest of the warps' ceil(k / warps)-th largest is a value that at least k
+// elements reach.
+//
+// At the end of a row the exact top-k is sorted and the survivor decision runs in double precision
+// on one warp (select_topk.cuh), in exactly the oracle's operation order. Bound: HBM bandwidth.
+#include "select_internal.h"
+#include "select_rows.cuh"
+#include "select_stream.cuh"
+#include "select_topk.cuh"
+
+namespace loom_select {
+
+namespace {
+
+constexpr int kSampWarps = 8;
+constexpr int kSampNT = kSampWarps * 32;
+constexpr int kSampStages = 4;
+constexpr int kSampStageBytes = 32768;
+constexpr int kCandCap = 4096;    // candidate keys in shared memory
+constexpr int kPruneAt = 2048;    // prune after a stage when more than this many are held
+constexpr int kDecideOffset = 1024; // e[] and S[] of the decision live past the first 1024 keys
+static_assert(kCandCap - kPruneAt >= kMaxHistory, "penalised entries of one stage must fit");
+static_assert(LOOM_SELECT_MAX_TOP_K <= kDecideOffset && 3 * kDecideOffset <= kCandCap,
+              "decision scratch (e at key slot 1024, S at 2048) overlaps the keys");
+
+struct SampleDev {
+    float T, r, p;
+    int32_t k;
+    bool greedy, penalty, lse, shard;
+    int64_t vocab_offset, vocab_limit;
+    const int32_t* hist;
+    int32_t hist_len;
+    const float* u;
+    int32_t* out_ids;
+    float* out_prob;
+    float* out_logp;
+    int32_t* out_topk;
+    unsigned char* shard_out; // [rows] records of loom_shard_record_bytes(k) (pairs)
+    unsigned char* recs;      // workspace records [2 * ctas] (keys), see record_slot
+    size_t rec_bytes;         // 16 + 8k
+    int* tickets;
+    int* status;
+};
+
+struct RecordHead {
+    int32_t count; // -1: the row has a bad history id
+    float m;
+    float s;
+    int32_t reserved;
+};
+
+struct SampleShared {
+    TopkShared tk;
+    int cnt;
+    int fail;
+    int bad;
+    int pen_cnt;
+    uint32_t warm_key;
+    float X;
+    float thr_y;
+    int last;
+    uint32_t min_key_hi;
+    LseAcc lse_w[kSampWarps];
+    LseAcc seg_lse;
+    int nan_tot[kSampWarps];
+    int nan_have;
+    int32_t sel_id;
+    float sel_prob;
+    float sel_y;
+};
+
+__device__ __forceinline__ float neg_inf() { return -__int_as_float(0x7f800000); }
+
+__device__ __forceinline__ float penalise(float x, float r) { return x > 0.0f ? __fdiv_rn(x, r) : __fmul_rn(x, r); }
+
+// Descending bitonic sort of one float per lane across the warp.
+__device__ __forceinline__ float warp_sort_desc(float v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, v, stride);
+            const bool lower = (lane & stride) == 0;
+            const bool desc = (lane & size) == 0;
+            v = (lower == desc) ? fmaxf(v, o) : fminf(v, o);
+        }
+    }
+    return v;
+}
+
+template <int kDtype>
+__device__ __forceinline__ float smem_elem(const unsigned char* data, int32_t i) {
+    if constexpr (kDtype == LOOM_SELECT_BF16) {
+        return bf16_bits_to_float(reinterpret_cast<const unsigned short*>(data)[i]);
+    } else {
+        return reinterpret_cast<const float*>(data)[i];
+    }
+}
+
+// After a prune: the value of the worst kept key becomes the threshold (only once k are kept).
+template <int kNT>
+__device__ void raise_threshold(const SampleDev& p, uint64_t* cand, int K, SampleShared* sh) {
+    if (K < p.k) return;
+    uint32_t mn = 0xffffffffu;
+    for (int i = threadIdx.x; i < K; i += kNT) {
+        const uint32_t hi = static_cast<uint32_t>(cand[i] >> 32);
+        mn = hi < mn ? hi : mn;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const uint32_t o = __shfl_xor_sync(0xffffffffu, mn, off);
+        mn = o < mn ? o : mn;
+    }
+    if (threadIdx.x == 0) sh->min_key_hi = 0xffffffffu;
+    group_sync<kNT>();
+    if ((threadIdx.x & 31) == 0) atomicMin(&sh->min_key_hi, mn);
+    group_sync<kNT>();
+    if (threadIdx.x == 0) {
+        const float t = order_key_to_float(sh->min_key_hi);
+        if (t > sh->thr_y) {
+            sh->thr_y = t;
+            sh->X = inverse_threshold(t, p.T, p.greedy);
+        }
+    }
+    group_sync<kNT>();
+}
+
+// Sorts the K (<= k) kept keys of a whole row, fills up to k with NaN ids when the row has fewer
+// than k non-NaN values, and emits the row's result (a decision, or a shard record).
+template <int kDtype, int kNT>
+__device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t row, uint64_t* cand, int K, LseAcc lse,
+                             bool bad, SampleShared* sh) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
+    const unsigned char* rowp = g.base + row * g.row_stride * kEsz;
+    if (bad) {
+        if (p.shard) {
+            if (tid == 0) {
+                RecordHead* h = reinterpret_cast<RecordHead*>(p.shard_out + row * p.rec_bytes);
+                h->count = -1;
+                h->m = __int_as_float(0x7fc00000);
+                h->s = __int_as_float(0x7fc00000);
+                h->reserved = 0;
+            }
+        } else {
+            if (tid == 0) {
+                p.out_ids[row] = -1;
+                p.out_prob[row] = __int_as_float(0x7fc00000);
+                if (p.out_logp) p.out_logp[row] = __int_as_float(0x7fc00000);
+            }
+            if (p.out_topk)
+                for (int j = tid; j < p.k; j += kNT) p.out_topk[row * p.k + j] = -1;
+        }
+        group_sync<kNT>();
+        return;
+    }
+    const int kk = static_cast<int>(p.k < g.width ? p.k : g.width); // a shard may be narrower than k
+    if (K < kk) {
+        // NaN fill in column order: NaN ranks below everything, lower id first
+        if (tid == 0) sh->nan_have = K;
+        group_sync<kNT>();
+        for (int64_t base = 0; base < g.width; base += kNT) {
+            const int have = sh->nan_have;
+            if (have >= kk) break;
+            const int64_t col = base + tid;
+            bool isn = false;
+            if (col < g.width) {
+                const float x = load_global_elem<kDtype>(rowp, col);
+                isn = x != x;
+            }
+            const uint32_t ballot = __ballot_sync(0xffffffffu, isn);
+            if (lane == 0) sh->nan_tot[warp] = __popc(ballot);
+            group_sync<kNT>();
+            int before = 0, total = 0;
+            for (int w = 0; w < kSampWarps; ++w) {
+                if (w < warp) before += sh->nan_tot[w];
+                total += sh->nan_tot[w];
+            }
+            if (isn) {
+                const int pos = have + before + __popc(ballot & ((1u << lane) - 1u));
+                if (pos < kk) cand[pos] = loom_rank_key(__int_as_float(0x7fc00000), static_cast<int32_t>(p.vocab_offset + col));
+            }
+            group_sync<kNT>();
+            if (tid == 0) sh->nan_have = have + total;
+            group_sync<kNT>();
+        }
+        K = kk;
+    }
+    const int P = next_pow2(K);
+    topk_sort_desc<kNT>(cand, K, P);
+    if (p.shard) {
+        unsigned char* rec = p.shard_out + row * p.rec_bytes;
+        if (tid == 0) {
+            RecordHead* h = reinterpret_cast<RecordHead*>(rec);
+            h->count = K;
+            h->m = lse.m;
+            h->s = lse.s;
+            h->reserved = 0;
+        }
+        uint2* pairs = reinterpret_cast<uint2*>(rec + 16);
+        for (int j = tid; j < K; j += kNT) {
+            const uint64_t key = cand[j];
+            pairs[j] = make_uint2(__float_as_uint(rank_key_value(key)), static_cast<uint32_t>(rank_key_id(key)));
+        }
+        group_sync<kNT>();
+        return;
+    }
+    if (warp == 0) {
+        double* e = reinterpret_cast<double*>(cand + kDecideOffset);
+        double* S = e + kDecideOffset;
+        if (p.greedy) {
+            if (lane == 0) {
+                const float x0 = load_global_elem<kDtype>(rowp, 0);
+                if (x0 != x0) {
+                    sh->sel_id = static_cast<int32_t>(p.vocab_offset);
+                    sh->sel_y = x0;
+                } else {
+                    sh->sel_id = rank_key_id(cand[0]);
+                    sh->sel_y = rank_key_value(cand[0]);
+                }
+                sh->sel_prob = 1.0f;
+            }
+        } else {
+            decide_warp(cand, K, p.p, __ldg(p.u + row), e, S, &sh->sel_id, &sh->sel_prob, &sh->sel_y);
+        }
+        if (lane == 0) {
+            p.out_ids[row] = sh->sel_id;
+            p.out_prob[row] = sh->sel_prob;
+            if (p.out_logp) {
+                const double lp = static_cast<double>(sh->sel_y) -
+                                  (static_cast<double>(lse.m) + log(static_cast<double>(lse.s)));
+                p.out_logp[row] = static_cast<float>(lp);
+            }
+        }
+    }
+    if (p.out_topk)
+        for (int j = tid; j < p.k; j += kNT) p.out_topk[row * p.k + j] = rank_key_id(cand[j]);
+    group_sync<kNT>();
+}
+
+template <int kDtype>
+struct SampleOp {
+    static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
+    static constexpr int kPer = 16 / kEsz;
+    static constexpr int kNT = kSampNT;
+    const StreamGeom& g;
+    const SampleDev& p;
+    SampleShared* sh;
+    uint64_t* cand;
+    uint32_t* bitmap;
+    int32_t* pen;
+    LseAcc lse;
+    bool first_chunk;
+
+    __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
+    __device__ const int32_t* row_hist(int64_t row) const { return p.hist + row * static_cast<int64_t>(p.hist_len); }
+
+    __device__ void begin_segment(const Segment& s) {
+        const int tid = threadIdx.x;
+        if (tid == 0) {
+            sh->cnt = 0;
+            sh->fail = 0x7fffffff;
+            sh->bad = 0;
+            sh->X = neg_inf();
+            sh->thr_y = neg_inf();
+            sh->warm_key = 0xffffffffu;
+        }
+        lse = lse_init();
+        first_chunk = true;
+        group_sync<kNT>();
+        if (p.hist_len > 0) {
+            const int32_t* h = row_hist(s.row);
+            for (int j = tid; j < p.hist_len; j += kNT) {
+                const int32_t id = __ldg(h + j);
+                if (id < 0 || id >= p.vocab_limit) sh->bad = 1;
+            }
+        }
+        const int32_t n_edges = segment_edge_count(s, kEsz);
+        if (tid < n_edges) {
+            const int64_t col = segment_edge_col(s, kEsz, tid);
+            float x = load_global_elem<kDtype>(row_ptr(s.row), col);
+            const int64_t gid = p.vocab_offset + col;
+            if (p.penalty) {
+                const int32_t* h = row_hist(s.row);
+                bool in = false;
+                for (int j = 0; j < p.hist_len && !in; ++j) in = (__ldg(h + j) == gid);
+                if (in) x = penalise(x, p.r);
+            }
+            const float y = tempered(x, p.T, p.greedy);
+            if (p.lse) lse_offer(lse, y);
+            if (y == y) cand[atomicAdd(&sh->cnt, 1)] = loom_rank_key(y, static_cast<int32_t>(gid));
+        }
+        group_sync<kNT>();
+        if (tid == 0 && sh->bad) record_status(p.status, LOOM_SELECT_EHISTORY);
+    }
+
+    __device__ void chunk(const Segment& s, const unsigned char* data, int64_t col0, int32_t n) {
+        const int tid = threadIdx.x, lane = tid & 31;
+        const int32_t nvec = n / kPer;
+        const uint4* v4 = reinterpret_cast<const uint4*>(data);
+        const int64_t gid0 = p.vocab_offset + col0;
+        const bool use_pen = p.penalty;
+
+        // 1. history ids inside this stage: mark them, list each distinct one once
+        if (use_pen) {
+            const int32_t nwords = (n + 31) >> 5;
+            for (int w = tid; w < nwords; w += kNT) bitmap[w] = 0u;
+            if (tid == 0) sh->pen_cnt = 0;
+            group_sync<kNT>();
+            const int32_t* h = row_hist(s.row);
+            for (int j = tid; j < p.hist_len; j += kNT) {
+                const int64_t c = static_cast<int64_t>(__ldg(h + j)) - gid0;
+                if (c >= 0 && c < n) {
+                    const uint32_t bit = 1u << (c & 31);
+                    const uint32_t old = atomicOr(&bitmap[c >> 5], bit);
+                    if (!(old & bit)) pen[atomicAdd(&sh->pen_cnt, 1)] = static_cast<int32_t>(c);
+                }
+            }
+            group_sync<kNT>();
+        }
+
+        // 2. seed the threshold from the segment's first stage
+        if (first_chunk) {
+            first_chunk = false;
+            float m = neg_inf();
+            for (int32_t v = tid; v < nvec; v += kNT) {
+                Vec16<kDtype> e;
+                e.unpack(v4[v]);
+                uint32_t hb = 0;
+                if (use_pen) hb = bitmap[(v * kPer) >> 5] >> ((v * kPer) & 31);
+#pragma unroll
+                for (int q = 0; q < kPer; ++q)
+                    if (!((hb >> q) & 1u)) m = fmaxf(m, e.x[q]);
+            }
+            const float sorted = warp_sort_desc(m);
+            const int q = (p.k + kSampWarps - 1) / kSampWarps;
+            const float bw = q <= 32 ? __shfl_sync(0xffffffffu, sorted, q - 1) : neg_inf();
+            if (lane == 0) atomicMin(&sh->warm_key, loom_order_key(bw));
+            group_sync<kNT>();
+            if (tid == 0) {
+                const float tx = order_key_to_float(sh->warm_key);
+                const float ty = tempered(tx, p.T, p.greedy);
+                if (ty > sh->thr_y) {
+                    sh->thr_y = ty;
+                    sh->X = inverse_threshold(ty, p.T, p.greedy);
+                }
+            }
+            group_sync<kNT>();
+        }
+
+        // 3. the penalised history entries of this stage
+        if (use_pen) {
+            const int pc = sh->pen_cnt;
+            const float thr = sh->thr_y;
+            for (int j = tid; j < pc; j += kNT) {
+                const int32_t c = pen[j];
+                const float y = tempered(penalise(smem_elem<kDtype>(data, c), p.r), p.T, p.greedy);
+                if (p.lse) lse_offer(lse, y);
+                if (y == y && y >= thr) cand[atomicAdd(&sh->cnt, 1)] = loom_rank_key(y, static_cast<int32_t>(gid0 + c));
+            }
+            // (buffer room: cnt <= kPruneAt before the stage and pc <= kMaxHistory)
+        }
+
+        // 4. the stream: compare against X, append the few that pass; prune and resume when full
+        const int32_t nrows = (nvec + kNT - 1) / kNT;
+        int32_t my_row = 0;
+        for (;;) {
+            const float X = sh->X;
+            for (; my_row < nrows; ++my_row) {
+                const int32_t v = my_row * kNT + tid;
+                const bool valid = v < nvec;
+                Vec16<kDtype> e;
+                uint32_t hb = 0;
+                uint32_t mask = 0;
+                if (valid) {
+                    e.unpack(v4[v]);
+                    if (use_pen) hb = bitmap[(v * kPer) >> 5] >> ((v * kPer) & 31);
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q)
+                        if (!((hb >> q) & 1u) && e.x[q] >= X) mask |= 1u << q;
+                }
+                if (__any_sync(0xffffffffu, mask != 0u)) {
+                    const int np = __popc(mask);
+                    int incl = np;
+#pragma unroll
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+                        if (lane >= off) incl += o;
+                    }
+                    const int total = __shfl_sync(0xffffffffu, incl, 31);
+                    int base = 0;
+                    if (lane == 31) base = atomicAdd(&sh->cnt, total);
+                    base = __shfl_sync(0xffffffffu, base, 31);
+                    if (base + total > kCandCap) {
+                        if (lane == 0) atomicMin(&sh->fail, base);
+                        break; // this row again after the prune
+                    }
+                    int pos = base + incl - np;
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q) {
+                        if ((mask >> q) & 1u) {
+                            const float y = tempered(e.x[q], p.T, p.greedy);
+                            cand[pos++] = loom_rank_key(y, static_cast<int32_t>(gid0 + v * kPer + q));
+                        }
+                    }
+                }
+                if (p.lse && valid) {
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q)
+                        if (!((hb >> q) & 1u)) lse_offer(lse, tempered(e.x[q], p.T, p.greedy));
+                }
+            }
+            group_sync<kNT>();
+            const int fail = sh->fail;
+            const int cnt = sh->cnt;
+            const bool finished = fail == 0x7fffffff;
+            if (finished && cnt <= kPruneAt) break;
+            const int held = cnt < fail ? cnt : fail;
+            group_sync<kNT>();
+            const int K = topk_select_compact<kNT, kCandCap / kNT>(cand, held, p.k, &sh->tk);
+            if (threadIdx.x == 0) {
+                sh->cnt = K;
+                sh->fail = 0x7fffffff;
+            }
+            raise_threshold<kNT>(p, cand, K, sh);
+            if (finished) break;
+        }
+    }
+
+    __device__ void end_chunk(const Segment&) {}
+
+    __device__ void end_segment(const Segment& s) {
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        if (p.lse) {
+            const LseAcc w = lse_warp_reduce(lse);
+            if (lane == 0) sh->lse_w[warp] = w;
+        }
+        group_sync<kNT>();
+        if (tid == 0) {
+            LseAcc a = lse_init();
+            if (p.lse)
+                for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
+            sh->seg_lse = a;
+        }
+        group_sync<kNT>();
+        const int cnt = sh->cnt;
+        const int K = topk_select_compact<kNT, kCandCap / kNT>(cand, cnt, p.k, &sh->tk);
+        const LseAcc seg = sh->seg_lse;
+        const bool bad = sh->bad != 0;
+        if (s.count == 1) {
+            finalize_row<kDtype, kNT>(p, g, s.row, cand, K, seg, bad, sh);
+            return;
+        }
+        // a piece of a split row: write its record, take a ticket, the last one merges
+        unsigned char* rec = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + s.index, s.row)) * p.rec_bytes;
+        uint64_t* keys = reinterpret_cast<uint64_t*>(rec + 16);
+        for (int j = tid; j < K; j += kNT) keys[j] = cand[j];
+        if (tid == 0) {
+            RecordHead* h = reinterpret_cast<RecordHead*>(rec);
+            h->count = bad ? -1 : K;
+            h->m = seg.m;
+            h->s = seg.s;
+            h->reserved = 0;
+        }
+        __threadfence();
+        group_sync<kNT>();
+        if (tid == 0) {
+            const int prev = atomicAdd(&p.tickets[s.row], 1);
+            sh->last = prev == s.count - 1;
+        }
+        group_sync<kNT>();
+        if (!sh->last) return;
+        __threadfence();
+        // merge every piece's record
+        int have = 0;
+        bool any_bad = false;
+        LseAcc tot = lse_init();
+        for (int j = 0; j < s.count; ++j) {
+            const unsigned char* r = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j, s.row)) * p.rec_bytes;
+            const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
+            if (c < 0) {
+                any_bad = true;
+                continue;
+            }
+            LseAcc part;
+            part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
+            part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
+            tot = lse_merge(tot, part);
+            if (have + c > kCandCap) {
+                have = topk_select_compact<kNT, kCandCap / kNT>(cand, have, p.k, &sh->tk);
+            }
+            const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
+            for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
+            have += c;
+            group_sync<kNT>();
+        }
+        const int Kf = topk_select_compact<kNT, kCandCap / kNT>(cand, have, p.k, &sh->tk);
+        if (tid == 0) p.tickets[s.row] = 0;
+        finalize_row<kDtype, kNT>(p, g, s.row, cand, Kf, tot, any_bad, sh);
+    }
+};
+
+constexpr size_t kSampDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
+                                (kSampStageBytes / 2 / 32) * sizeof(uint32_t) + kMaxHistory * sizeof(int32_t);
+
+template <int kDtype>
+__global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel(StreamGeom g, SampleDev p) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    __shared__ StreamCtl ctl;
+    __shared__ SampleShared sh;
+    unsigned char* ring = dyn;
+    uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + static_cast<size_t>(kSampStages) * kSampStageBytes);
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(cand + kCandCap);
+    int32_t* pen = reinterpret_cast<int32_t*>(bitmap + kSampStageBytes / 2 / 32);
+    SampleOp<kDtype> op{g, p, &sh, cand, bitmap, pen, lse_init(), true};
+    stream_ranges<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
+}
+
+// ---------------------------------------------------------------------------------------------
+// K4: merge of the gathered shard records, one CTA per row.
+
+constexpr int kMergeNT = 256;
+
+__global__ void __launch_bounds__(kMergeNT) shard_merge_kernel(const unsigned char* records, int32_t n_shards,
+                                                               int64_t rows, size_t rec_bytes, const float* u,
+                                                               int32_t k, float top_p, int32_t* out_ids,
+                                                               float* out_prob, float* out_logp, int32_t* out_topk) {
+    extern __shared__ __align__(16) uint64_t mcand[];
+    __shared__ TopkShared tk;
+    __shared__ int bad;
+    __shared__ int32_t sel_id;
+    __shared__ float sel_prob, sel_y;
+    __shared__ float m_max;
+    const int64_t row = blockIdx.x;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        bad = 0;
+        float M = neg_inf();
+        for (int g = 0; g < n_shards; ++g) {
+            const RecordHead* h = reinterpret_cast<const RecordHead*>(records + (static_cast<size_t>(g) * rows + row) * rec_bytes);
+            if (h->count < 0) bad = 1;
+            else if (h->m > M) M = h->m;
+        }
+        m_max = M;
+    }
+    __syncthreads();
+    if (bad) {
+        if (tid == 0) {
+            out_ids[row] = -1;
+            out_prob[row] = __int_as_float(0x7fc00000);
+            if (out_logp) out_logp[row] = __int_as_float(0x7fc00000);
+        }
+        if (out_topk)
+            for (int j = tid; j < k; j += kMergeNT) out_topk[row * k + j] = -1;
+        return;
+    }
+    int have = 0;
+    const int cap = kCandCap;
+    for (int g = 0; g < n_shards; ++g) {
+        const unsigned char* rec = records + (static_cast<size_t>(g) * rows + row) * rec_bytes;
+        const int32_t c = reinterpret_cast<const RecordHead*>(rec)->count;
+        if (have + c > cap) have = topk_select_compact<kMergeNT, kCandCap / kMergeNT>(mcand, have, k, &tk);
+        const uint2* pairs = reinterpret_cast<const uint2*>(rec + 16);
+        for (int i = tid; i < c; i += kMergeNT) {
+            const uint2 pr = pairs[i];
+            mcand[have + i] = loom_rank_key(__uint_as_float(pr.x), static_cast<int32_t>(pr.y));
+        }
+        have += c;
+        __syncthreads();
+    }
+    const int K = topk_select_compact<kMergeNT, kCandCap / kMergeNT>(mcand, have, k, &tk);
+    topk_sort_desc<kMergeNT>(mcand, K, next_pow2(K));
+    if (tid < 32) {
+        double* e = reinterpret_cast<double*>(mcand + kDecideOffset);
+        double* S = e + kDecideOffset;
+        decide_warp(mcand, K, top_p, __ldg(u + row), e, S, &sel_id, &sel_prob, &sel_y);
+        if (tid == 0) {
+            out_ids[row] = sel_id;
+            out_prob[row] = sel_prob;
+            if (out_logp) {
+                const double M = m_max;
+                double S_all = 0.0;
+                for (int g = 0; g < n_shards; ++g) {
+                    const RecordHead* h = reinterpret_cast<const RecordHead*>(records + (static_cast<size_t>(g) * rows + row) * rec_bytes);
+                    if (h->s > 0.0f) S_all += static_cast<double>(h->s) * (static_cast<double>(h->m) == M ? 1.0 : exp(static_cast<double>(h->m) - M));
+                }
+                out_logp[row] = static_cast<float>(static_cast<double>(sel_y) - (M + log(S_all)));
+            }
+        }
+    }
+    if (out_topk)
+        for (int j = tid; j < k; j += kMergeNT) out_topk[row * k + j] = j < K ? rank_key_id(mcand[j]) : -1;
+}
+
+template <int kDtype>
+cudaError_t launch_sample_t(const StreamGeom& g, const SampleDev& p, cudaStream_t stream) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(sample_stream_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kSampDynSmem));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    sample_stream_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kSampDynSmem, stream>>>(g, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t sample_record_bytes(int32_t top_k) { return 16 + 8 * static_cast<size_t>(top_k); }
+
+cudaError_t launch_sample_stream(const SampleLaunch& a, void* workspace, const WsLayout& l, int ctas,
+                                 cudaStream_t stream) {
+    StreamGeom g;
+    g.base = static_cast<const unsigned char*>(a.logits);
+    g.rows = a.rows;
+    g.width = a.width;
+    g.row_stride = a.row_stride;
+    g.total = a.rows * a.width;
+    g.esz = a.dtype == LOOM_SELECT_BF16 ? 2 : 4;
+    g.ctas = ctas;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    SampleDev p;
+    p.T = a.temperature;
+    p.r = a.penalty;
+    p.p = a.top_p;
+    p.k = a.top_k;
+    p.greedy = a.temperature == 0.0f;
+    p.penalty = a.history_len > 0 && a.penalty != 1.0f;
+    p.shard = a.shard_out != nullptr;
+    p.lse = p.shard || a.out_logp != nullptr;
+    p.vocab_offset = a.vocab_offset;
+    p.vocab_limit = a.vocab_limit;
+    p.hist = a.history;
+    p.hist_len = a.history_len;
+    p.u = a.u;
+    p.out_ids = a.out_ids;
+    p.out_prob = a.out_prob;
+    p.out_logp = a.out_logp;
+    p.out_topk = a.out_topk;
+    p.shard_out = static_cast<unsigned char*>(a.shard_out);
+    p.recs = ws + l.records;
+    p.rec_bytes = sample_record_bytes(a.top_k);
+    p.tickets = reinterpret_cast<int*>(ws + l.tickets);
+    p.status = reinterpret_cast<int*>(ws);
+    if (a.dtype == LOOM_SELECT_BF16) return launch_sample_t<LOOM_SELECT_BF16>(g, p, stream);
+    return launch_sample_t<LOOM_SELECT_F32>(g, p, stream);
+}
+
+cudaError_t launch_shard_merge(const void* records, int32_t n_shards, int64_t rows, const float* u, int32_t top_k,
+                               float top_p, int32_t* out_ids, float* out_prob, float* out_logp, int32_t* out_topk,
+                               cudaStream_t stream) {
+    const size_t smem = kCandCap * sizeof(uint64_t);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    shard_merge_kernel<<<static_cast<unsigned>(rows), kMergeNT, smem, stream>>>(
+        static_cast<const unsigned char*>(records), n_shards, rows, sample_record_bytes(top_k), u, top_k, top_p, out_ids,
+        out_prob, out_logp, out_topk);
+    return cudaGetLastError();
+}
+
+}  // namespace loom_select
