@@ -82,7 +82,8 @@ struct ArgmaxOp {
             } else {
                 records[record_slot(g, s.first_cta + s.index, s.row)] = ArgRecord{b.v, b.i};
                 __threadfence();
-                const int prev = atomicAdd(&tickets[s.row], 1);
+                int* ticket = &tickets[record_slot(g, s.first_cta, s.row)];
+                const int prev = atomicAdd(ticket, 1);
                 if (prev == s.count - 1) {
                     __threadfence();
                     ArgBest m = arg_init();
@@ -93,7 +94,7 @@ struct ArgmaxOp {
                         arg_offer(m, v, i);
                     }
                     out_ids[s.row] = static_cast<int32_t>(lo + final_col(s.row, m));
-                    tickets[s.row] = 0;
+                    *ticket = 0;
                 }
             }
         }

@@ -72,7 +72,7 @@ int check_params(const loom_sample_params* p, int64_t vocab, bool allow_greedy) 
 }
 
 size_t sample_ws_bytes(int64_t rows, int32_t top_k) {
-    return ws_layout(rows, sample_record_bytes(top_k), kStreamRecordSlots).bytes;
+    return ws_layout(sample_record_bytes(top_k), kStreamRecordSlots).bytes;
 }
 
 }  // namespace
@@ -99,7 +99,7 @@ int loom_select_abi_version(void) { return 100; }
 
 size_t loom_argmax_workspace_size(int64_t rows, int64_t n_vocab) {
     if (rows <= 0 || n_vocab <= 0) return kWsAlign;
-    return ws_layout(rows, 8, kStreamRecordSlots).bytes;
+    return ws_layout(8, kStreamRecordSlots).bytes;
 }
 
 size_t loom_sample_workspace_size(int64_t rows, int64_t n_vocab, int32_t top_k) {
@@ -109,7 +109,7 @@ size_t loom_sample_workspace_size(int64_t rows, int64_t n_vocab, int32_t top_k) 
 
 size_t loom_ctc_workspace_size(int64_t n_utt, int64_t n_frames) {
     if (n_utt <= 0 || n_frames <= 0) return kWsAlign;
-    return ws_layout(n_utt, sizeof(int32_t), n_utt * n_frames).bytes;
+    return ws_layout(sizeof(int32_t), n_utt * n_frames).bytes;
 }
 
 size_t loom_shard_record_bytes(int32_t top_k) { return top_k > 0 ? sample_record_bytes(top_k) : 0; }
@@ -148,7 +148,7 @@ int loom_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     const void* base = static_cast<const unsigned char*>(logits) + lo * esz_of(dtype);
     if (width <= kShortRowMax) return map_cuda(launch_rows_argmax(dtype, base, rows, width, row_stride, lo, out_ids, sms, st));
-    const WsLayout l = ws_layout(rows, 8, kStreamRecordSlots);
+    const WsLayout l = ws_layout(8, kStreamRecordSlots);
     const int ctas = stream_ctas(rows * width, sms);
     return map_cuda(launch_argmax_stream(dtype, base, rows, width, row_stride, lo, out_ids, workspace, l, ctas, st));
 }
@@ -187,7 +187,7 @@ int loom_sample_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     a.out_logp = out_logp;
     a.out_topk = out_topk_ids;
     a.shard_out = nullptr;
-    const WsLayout l = ws_layout(rows, sample_record_bytes(params->top_k), kStreamRecordSlots);
+    const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
     return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * n_vocab, sms),
                                          static_cast<cudaStream_t>(stream)));
 }
@@ -222,7 +222,7 @@ int loom_sample_shard_partial(const void* logits, int dtype, int64_t rows, int64
     a.top_p = params->top_p;
     a.top_k = params->top_k;
     a.shard_out = out_records;
-    const WsLayout l = ws_layout(rows, sample_record_bytes(params->top_k), kStreamRecordSlots);
+    const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
     return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * shard_vocab, sms),
                                          static_cast<cudaStream_t>(stream)));
 }
@@ -244,12 +244,12 @@ int loom_ctc_greedy(const void* logits, int dtype, int64_t n_utt, int64_t n_fram
     if (!dtype_ok(dtype)) return LOOM_SELECT_EDTYPE;
     if (!logits || !out_ids || !out_frames || !out_len || n_utt <= 0 || n_frames <= 0 || n_classes <= 0)
         return LOOM_SELECT_EINVAL;
-    if (n_classes > INT32_MAX || n_frames > INT32_MAX) return LOOM_SELECT_ESHAPE;
+    if (n_classes > INT32_MAX || n_frames > INT32_MAX || n_utt > kCtcMaxUtt) return LOOM_SELECT_ESHAPE;
     if (int st = check_workspace(workspace, workspace_bytes, loom_ctc_workspace_size(n_utt, n_frames))) return st;
     int status = LOOM_SELECT_OK;
     const int sms = device_sm_count(&status);
     if (status) return status;
-    const WsLayout l = ws_layout(n_utt, sizeof(int32_t), n_utt * n_frames);
+    const WsLayout l = ws_layout(sizeof(int32_t), n_utt * n_frames);
     return map_cuda(launch_ctc(dtype, logits, n_utt, n_frames, n_classes, blank, out_ids, out_frames, out_len,
                                out_frame_ids, out_frame_logp, workspace, l, sms, static_cast<cudaStream_t>(stream)));
 }

@@ -4,9 +4,10 @@
 // ggml_backend_tensor_get + scan of argmax_tensor_rows (src/core/lua_bridge.cpp:343-365):
 //   1. per frame: argmax of the raw logits (strict '>' scan rule, NaN in column 0 wins), optionally
 //      its log-softmax value;
-//   2. per utterance, once all its frames are done (an atomic frame count per utterance; the CTA
-//      that completes it does the rest, nothing waits): keep frame f when id[f] != id[f-1] (id[-1] =
-//      blank) and id[f] != blank, then a block scan compacts the kept ids and their frame indices.
+//   2. per utterance, once all its frames are done (by the CTA holding it whole, or -- for an
+//      utterance split across CTAs -- by the CTA that completes its atomic frame count; nothing
+//      waits): keep frame f when id[f] != id[f-1] (id[-1] = blank) and id[f] != blank, then a block
+//      scan compacts the kept ids and their frame indices.
 // Each persistent CTA owns a contiguous, equal share of the n_utt * n_frames frames.
 // Bound: HBM bandwidth (one read of the logits; the per-frame ids are 4 bytes per frame).
 #include <cstdint>
@@ -45,12 +46,27 @@ __global__ void __launch_bounds__(kRowNT) rows_argmax_kernel(const unsigned char
 // ----------------------------------------------------------------------------------------------
 // CTC
 
+constexpr int kMaxUttPerCta = 64;
+static_assert(kCtcMaxUtt == kTicketSlots * (kMaxUttPerCta - 2), "CTC utterance bound");
+
 struct CtcShared {
     int n_last;
-    int64_t last_utt[4];
+    int64_t last_utt[kMaxUttPerCta];
+    int last_ticket[kMaxUttPerCta]; // -1: the utterance lies wholly in this CTA
     int warp_tot[kRowWarps];
     int carry;
 };
+
+// Frames are split evenly: CTA c owns [c * total / G, (c + 1) * total / G).
+__device__ __forceinline__ int64_t ctc_range_start(int64_t c, int64_t total, int64_t G) { return c * total / G; }
+
+__device__ __forceinline__ int64_t ctc_cta_of_frame(int64_t f, int64_t total, int64_t G) {
+    int64_t c = f * G / total;
+    if (c >= G) c = G - 1;
+    while (c + 1 < G && ctc_range_start(c + 1, total, G) <= f) ++c;
+    while (c > 0 && ctc_range_start(c, total, G) > f) --c;
+    return c;
+}
 
 // Compacts utterance u's kept frames. Called by the whole CTA.
 __device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const int32_t* frame_ids, int32_t* out_ids,
@@ -117,19 +133,31 @@ __global__ void __launch_bounds__(kRowNT) ctc_kernel(const unsigned char* logits
             }
         }
     }
-    // every frame of this CTA written -> count them into their utterances
+    // Every frame of this CTA is written. An utterance held whole here is collapsed here; one split
+    // across CTAs counts its frames on the ticket of the CTA holding its first frame (at most one
+    // split utterance starts in any CTA), and whichever CTA completes the count collapses it.
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
         sh.n_last = 0;
+        const int64_t G = gridDim.x;
         if (f_hi > f_lo) {
             const int64_t u0 = f_lo / n_frames, u1 = (f_hi - 1) / n_frames;
             for (int64_t u = u0; u <= u1; ++u) {
                 const int64_t a = u * n_frames > f_lo ? u * n_frames : f_lo;
                 const int64_t b = (u + 1) * n_frames < f_hi ? (u + 1) * n_frames : f_hi;
                 const int n = static_cast<int>(b - a);
-                const int prev = atomicAdd(&tickets[u], n);
-                if (prev + n == n_frames) sh.last_utt[sh.n_last++] = u;
+                if (n == n_frames) {
+                    sh.last_utt[sh.n_last] = u;
+                    sh.last_ticket[sh.n_last++] = -1;
+                    continue;
+                }
+                const int t = static_cast<int>(ctc_cta_of_frame(u * n_frames, total, G));
+                const int prev = atomicAdd(&tickets[t], n);
+                if (prev + n == n_frames) {
+                    sh.last_utt[sh.n_last] = u;
+                    sh.last_ticket[sh.n_last++] = t;
+                }
             }
         }
         __threadfence();
@@ -138,8 +166,9 @@ __global__ void __launch_bounds__(kRowNT) ctc_kernel(const unsigned char* logits
     const int n_last = sh.n_last;
     for (int j = 0; j < n_last; ++j) {
         const int64_t u = sh.last_utt[j];
+        const int t = sh.last_ticket[j];
         ctc_collapse(u, n_frames, blank, frame_ids, out_ids, out_frames, out_len, &sh);
-        if (threadIdx.x == 0) tickets[u] = 0;
+        if (threadIdx.x == 0 && t >= 0) tickets[t] = 0;
     }
 }
 
@@ -165,10 +194,12 @@ cudaError_t launch_ctc(int dtype, const void* logits, int64_t n_utt, int64_t n_f
     int* tickets = reinterpret_cast<int*>(ws + l.tickets);
     if (!frame_ids) frame_ids = reinterpret_cast<int32_t*>(ws + l.records);
     const int64_t total = n_utt * n_frames;
-    // a CTA spans at most 4 utterances: enough CTAs that each holds <= 3 utterances' frames
+    // enough CTAs that none holds more than kMaxUttPerCta - 2 whole utterances, at most one ticket
+    // slot per CTA (the caller checked n_utt <= kCtcMaxUtt)
     int64_t grid = static_cast<int64_t>(sms) * 4;
-    const int64_t min_grid = (n_utt + 2) / 3 + 1;
+    const int64_t min_grid = (n_utt + kMaxUttPerCta - 3) / (kMaxUttPerCta - 2);
     if (grid < min_grid) grid = min_grid;
+    if (grid > kTicketSlots) grid = kTicketSlots;
     if (grid > total) grid = total;
     const unsigned char* base = static_cast<const unsigned char*>(logits);
     const bool lp = frame_logp != nullptr;

@@ -10,9 +10,11 @@
 namespace loom_select {
 
 // ---- workspace layout (every region 256-byte aligned) ----
-//   [0, 256)            status word (int32) of the device-side error report
-//   tickets             one int32 per row (or utterance), zero between calls
-//   records / frames    per-call scratch, fully written before it is read
+//   [0, 256)              status word (int32) of the device-side error report
+//   [256, 256 + 8 KiB)    tickets: kTicketSlots int32 at a FIXED place for every call, zero between
+//                         calls (each kernel returns the tickets it used to zero), so calls of any
+//                         size and kind can share one workspace
+//   records / frames      per-call scratch, fully written before it is read
 constexpr size_t kWsAlign = 256;
 inline size_t ws_round(size_t b) { return (b + kWsAlign - 1) / kWsAlign * kWsAlign; }
 
@@ -22,7 +24,12 @@ constexpr int kStreamMaxCtas = 1024;
 
 // A CTA's range splits at most two rows (its first and its last), so a streamed call needs at
 // most two partial-result records per CTA: slot 0 for the CTA's first row, slot 1 for its last.
+// A split row counts its pieces on the ticket of its first piece's slot.
 constexpr int64_t kStreamRecordSlots = 2 * kStreamMaxCtas;
+constexpr int64_t kTicketSlots = 2 * kStreamMaxCtas;
+
+// CTC: a CTA holds at most 62 whole utterances and the grid at most kTicketSlots CTAs.
+constexpr int64_t kCtcMaxUtt = kTicketSlots * 62;
 
 struct WsLayout {
     size_t tickets = 0;
@@ -30,10 +37,10 @@ struct WsLayout {
     size_t bytes = 0;
 };
 
-inline WsLayout ws_layout(int64_t n_tickets, size_t record_bytes, int64_t n_records) {
+inline WsLayout ws_layout(size_t record_bytes, int64_t n_records) {
     WsLayout l;
     l.tickets = kWsAlign;
-    l.records = l.tickets + ws_round(static_cast<size_t>(n_tickets) * sizeof(int32_t));
+    l.records = l.tickets + ws_round(static_cast<size_t>(kTicketSlots) * sizeof(int32_t));
     l.bytes = l.records + ws_round(record_bytes * static_cast<size_t>(n_records));
     return l;
 }

@@ -52,7 +52,7 @@ struct SampleDev {
     unsigned char* shard_out; // [rows] records of loom_shard_record_bytes(k) (pairs)
     unsigned char* recs;      // workspace records [2 * ctas] (keys), see record_slot
     size_t rec_bytes;         // 16 + 8k
-    int* tickets;
+    int* tickets;             // [2 * ctas]: a split row's ticket is its first piece's record slot
     int* status;
 };
 
@@ -480,7 +480,7 @@ struct SampleOp {
         __threadfence();
         group_sync<kNT>();
         if (tid == 0) {
-            const int prev = atomicAdd(&p.tickets[s.row], 1);
+            const int prev = atomicAdd(&p.tickets[record_slot(g, s.first_cta, s.row)], 1);
             sh->last = prev == s.count - 1;
         }
         group_sync<kNT>();
@@ -510,7 +510,7 @@ struct SampleOp {
             group_sync<kNT>();
         }
         const int Kf = topk_select_compact<kNT, kCandCap / kNT>(cand, have, p.k, &sh->tk);
-        if (tid == 0) p.tickets[s.row] = 0;
+        if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
         finalize_row<kDtype, kNT>(p, g, s.row, cand, Kf, tot, any_bad, sh);
     }
 };

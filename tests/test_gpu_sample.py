@@ -170,3 +170,22 @@ def test_repeat_calls_same_result(sel, dev):
         for key in ("ids", "topk", "prob"):
             np.testing.assert_array_equal(first[key], again[key])
     assert ws.read_status() == sel.OK
+
+
+def test_one_workspace_for_calls_of_every_size(sel, dev, oracle):
+    # One workspace serves calls of any size and kind: growing and shrinking row counts, another k,
+    # argmax and CTC calls in between (the tickets must stay where every call expects them).
+    ws = sel.Workspace(dev)
+    for rows, k in [(16, 40), (128, 40), (1, 64), (149, 1024), (2, 40), (128, 40), (5, 3)]:
+        x, hist, u = synth.sample_chain(rows, seed=rows + k, device="cuda")
+        vs_oracle(sel, oracle, x, hist, u, 0.7, 1.1, k, 0.9, workspace=ws)
+        out = torch.empty(rows, dtype=torch.int32, device=dev)
+        sel.argmax_rows_into(x, out, workspace=ws)
+        np.testing.assert_array_equal(out.cpu().numpy(), oracle.argmax_rows(x.cpu().numpy(), nthreads=NT))
+        f = synth.ctc_frames(3, 500 + rows, seed=rows, device="cuda")
+        ids, frames, lens = sel.ctc_greedy(f, synth.CTC_BLANK, workspace=ws)
+        seqs, _, _ = oracle.ctc_greedy(f.cpu().numpy(), synth.CTC_BLANK, nthreads=NT)
+        for utt, (wi, wf) in enumerate(seqs):
+            n = int(lens[utt].item())
+            np.testing.assert_array_equal(ids[utt, :n].cpu().numpy(), wi)
+    assert ws.read_status() == sel.OK
