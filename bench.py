@@ -330,7 +330,7 @@ def run_b200(args):
     avg_ms = max_over_ranks(sum(per_launch_ms) / len(per_launch_ms), world)
 
     e2e_obj = None
-    if e2e is not None:
+    if e2e is not None and not args.no_e2e:
         fn, h2d, d2h = e2e
         for i in range(2):
             fn(i)
@@ -380,6 +380,11 @@ def run_b200(args):
     return 0
 
 
+def set_rows(n):
+    global ROWS
+    ROWS = n
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,9 +393,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="sample", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
+    ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling a smaller case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    set_rows(args.rows)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

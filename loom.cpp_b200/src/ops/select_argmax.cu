@@ -30,34 +30,58 @@ template <int kDtype>
 struct ArgmaxOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     static constexpr int kPer = 16 / kEsz;
+    static constexpr int kU = 4; // vectors per thread per step
     const StreamGeom& g;
     int64_t lo;
     int32_t* out_ids;
     ArgRecord* records;
     int* tickets;
     ArgShared* sh;
-    ArgBest best;
+    ArgBest best; // the WARP's best so far: identical in every lane
 
     __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
 
-    __device__ void begin_segment(const Segment& s) {
-        best = arg_init();
-        const int32_t n_edges = segment_edge_count(s, kEsz);
-        if (static_cast<int>(threadIdx.x) < n_edges) {
-            const int64_t col = segment_edge_col(s, kEsz, threadIdx.x);
-            arg_offer(best, load_global_elem<kDtype>(row_ptr(s.row), col), static_cast<int32_t>(col));
-        }
-    }
+    __device__ void begin_segment(const Segment&) { best = arg_init(); }
 
+    // Steps of kU vectors per thread, columns increasing from step to step. A step can change the
+    // warp's best only where some element reaches it (or, before anything is taken, equals -inf);
+    // then the lanes' own bests join the warp's in one reduction (value desc, column asc).
     __device__ void chunk(const Segment&, const unsigned char* data, int64_t col0, int32_t n) {
+        constexpr int kNT = kArgNT;
         const int32_t nvec = n / kPer;
         const uint4* v4 = reinterpret_cast<const uint4*>(data);
-        for (int32_t v = threadIdx.x; v < nvec; v += kArgNT) {
-            Vec16<kDtype> e;
-            e.unpack(v4[v]);
-            const int32_t col = static_cast<int32_t>(col0) + v * kPer;
+        const int32_t nsteps = (nvec + kU * kNT - 1) / (kU * kNT);
+        for (int32_t step = 0; step < nsteps; ++step) {
+            const int32_t v0 = step * kU * kNT + static_cast<int32_t>(threadIdx.x);
+            Vec16<kDtype> e[kU];
+            float mu = __int_as_float(0x7fc00000); // NaN: fmaxf skips it
 #pragma unroll
-            for (int q = 0; q < kPer; ++q) arg_offer(best, e.x[q], col + q);
+            for (int u = 0; u < kU; ++u) {
+                const int32_t v = v0 + u * kNT;
+                if (v < nvec) {
+                    e[u].unpack(v4[v]);
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q) mu = fmaxf(mu, e[u].x[q]);
+                }
+            }
+            const bool take = mu > best.v || (mu == best.v && best.i == 0x7fffffff);
+            if (__any_sync(0xffffffffu, take)) {
+                ArgBest b = arg_init();
+                if (take) {
+#pragma unroll
+                    for (int u = 0; u < kU; ++u) {
+                        const int32_t v = v0 + u * kNT;
+                        if (v < nvec) {
+                            const int32_t col = static_cast<int32_t>(col0) + v * kPer;
+#pragma unroll
+                            for (int q = 0; q < kPer; ++q) arg_offer(b, e[u].x[q], col + q);
+                        }
+                    }
+                }
+                b = arg_warp_reduce(b);
+                arg_offer(b, best.v, best.i);
+                best = b;
+            }
         }
     }
 
@@ -71,7 +95,16 @@ struct ArgmaxOp {
 
     __device__ void end_segment(const Segment& s) {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-        ArgBest b = arg_warp_reduce(best);
+        // the edges (outside the aligned interior, at both ends of the columns) join last: the
+        // final combine orders by value, then column, whatever the order things were seen in
+        ArgBest b = arg_init();
+        const int32_t n_edges = segment_edge_count(s, kEsz);
+        if (static_cast<int>(threadIdx.x) < n_edges) {
+            const int64_t col = segment_edge_col(s, kEsz, threadIdx.x);
+            arg_offer(b, load_global_elem<kDtype>(row_ptr(s.row), col), static_cast<int32_t>(col));
+        }
+        b = arg_warp_reduce(b);
+        arg_offer(b, best.v, best.i);
         if (lane == 0) sh->red[warp] = b;
         group_sync<kArgNT>();
         if (threadIdx.x == 0) {

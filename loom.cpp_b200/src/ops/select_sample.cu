@@ -1,22 +1,25 @@
 // select_sample.cu -- the fused sampling chain (K2) and the vocabulary-shard merge (K4).
 //
-// One pass over the logits: rows stream through shared memory (select_stream.cuh); per element the
-// only work is a compare of the raw logit against a threshold X. X is exact: it is the smallest x
-// whose tempered value x / T reaches the current k-th best tempered value, so every element below
-// it is strictly worse than k elements already kept. The few elements that pass are tempered with
-// an IEEE divide and appended to a shared-memory candidate buffer of 64-bit rank keys; when the
-// buffer fills, a radix select keeps the exact top-k and raises X.
+// One pass over the logits: rows stream through shared memory (select_stream.cuh). The per-element
+// work is a compare: every thread takes 4 vectors of 16 bytes per step, and one warp vote asks
+// whether any maximum reaches a threshold X. X is exact -- the smallest raw value whose tempered
+// value x / T reaches the current k-th best tempered value -- so every element below it is strictly
+// worse than k elements already kept. The rare elements that pass go, raw, into their warp's own
+// region of shared memory (offsets from ballots, a register counter: no atomics, no divides).
 //
-// The repetition penalty touches only the history ids. They are marked in a per-stage bitmap: the
-// stream skips them and they are inserted separately with their penalised, tempered value, which
-// keeps the per-element path free of the penalty.
+// At the end of a stage, when more than k + kPruneSlack candidates are held, they are tempered with
+// an IEEE divide (in parallel), the exact top-k is kept as 64-bit rank keys, and X rises to the k-th.
+// The first stage of each row segment seeds X: each warp sorts its lanes' maxima and the smallest of
+// the warps' ceil(k / warps)-th largest is a value that at least k elements reach.
 //
-// The first stage of every row segment seeds X from the stage itself: each warp sorts its lanes'
-// maxima, and the smallest of the warps' ceil(k / warps)-th largest is a value that at least k
-// elements reach.
+// The repetition penalty touches only the history ids: at the start of a row segment the distinct
+// ones inside it go into a shared-memory hash set and are inserted once, with their penalised,
+// tempered values read from global memory; the stream skips set members (looked up only for
+// elements that pass X). So the per-element path carries no penalty work.
 //
-// At the end of a row the exact top-k is sorted and the survivor decision runs in double precision
-// on one warp (select_topk.cuh), in exactly the oracle's operation order. Bound: HBM bandwidth.
+// At the end of a row the exact top-k is ranked into order and the survivor decision runs in double
+// precision on one warp (select_topk.cuh), in exactly the oracle's operation order.
+// Bound: HBM bandwidth (4 bytes per f32 logit, 2 per bf16, read once).
 #include "select_internal.h"
 #include "select_rows.cuh"
 #include "select_stream.cuh"
@@ -30,12 +33,18 @@ constexpr int kSampWarps = 8;
 constexpr int kSampNT = kSampWarps * 32;
 constexpr int kSampStages = 4;
 constexpr int kSampStageBytes = 32768;
-constexpr int kCandCap = 4096;    // candidate keys in shared memory
-constexpr int kPruneAt = 2048;    // prune after a stage when more than this many are held
-constexpr int kDecideOffset = 1024; // e[] and S[] of the decision live past the first 1024 keys
-static_assert(kCandCap - kPruneAt >= kMaxHistory, "penalised entries of one stage must fit");
-static_assert(LOOM_SELECT_MAX_TOP_K <= kDecideOffset && 3 * kDecideOffset <= kCandCap,
-              "decision scratch (e at key slot 1024, S at 2048) overlaps the keys");
+constexpr int kCandCap = 4096;    // candidate rank keys in shared memory
+constexpr int kRawPerWarp = 256;  // raw candidates a warp holds between prunes
+constexpr int kPruneSlack = 64;   // prune at a stage end when more than k + this many are held
+constexpr int kHashSlots = 4096;  // history hash set (load <= 1/2 at kMaxHistory ids)
+constexpr int kDecideSlots = 1024;
+constexpr int kStepVecs = 4;      // vectors per thread per step of the stream
+static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kSampWarps * kRawPerWarp, "a prune's keys must fit");
+static_assert(kCandCap >= kMaxHistory + 16, "a segment's penalised entries and edges must fit");
+static_assert(LOOM_SELECT_MAX_TOP_K <= kDecideSlots && 2 * kDecideSlots <= kCandCap,
+              "decision scratch e[] lives in key slots [1024, 2048)");
+static_assert(2 * kMaxHistory <= kHashSlots, "hash set load");
+static_assert(kRawPerWarp >= 32 * 8, "one vector's passes (32 lanes x 8 bf16) must fit an empty warp region");
 
 struct SampleDev {
     float T, r, p;
@@ -65,15 +74,14 @@ struct RecordHead {
 
 struct SampleShared {
     TopkShared tk;
-    int cnt;
-    int fail;
+    int K;         // rank keys held in cand[0, K)
+    int fail;      // a warp's raw region filled up mid-stage
     int bad;
-    int pen_cnt;
     uint32_t warm_key;
     float X;
     float thr_y;
     int last;
-    uint32_t min_key_hi;
+    int wcnt[kSampWarps];
     LseAcc lse_w[kSampWarps];
     LseAcc seg_lse;
     int nan_tot[kSampWarps];
@@ -112,39 +120,74 @@ __device__ __forceinline__ float smem_elem(const unsigned char* data, int32_t i)
     }
 }
 
-// After a prune: the value of the worst kept key becomes the threshold (only once k are kept).
+// History hash set: open addressing over global ids, -1 = empty.
+__device__ __forceinline__ uint32_t hash_slot(int32_t id) {
+    return (static_cast<uint32_t>(id) * 2654435761u) >> (32 - 12);  // 4096 slots
+}
+
+__device__ __forceinline__ bool hash_contains(const int32_t* set, int32_t id) {
+    uint32_t h = hash_slot(id);
+    for (int probe = 0; probe < kHashSlots; ++probe) {
+        const int32_t v = set[h];
+        if (v == id) return true;
+        if (v < 0) return false;
+        h = (h + 1) & (kHashSlots - 1);
+    }
+    return false;
+}
+
+// Inserts id; true if it was not there yet.
+__device__ __forceinline__ bool hash_insert(int32_t* set, int32_t id) {
+    uint32_t h = hash_slot(id);
+    for (int probe = 0; probe < kHashSlots; ++probe) {
+        const int32_t old = atomicCAS(&set[h], -1, id);
+        if (old == -1) return true;
+        if (old == id) return false;
+        h = (h + 1) & (kHashSlots - 1);
+    }
+    return false;
+}
+
+// Tempers every warp's raw candidates into rank keys after the held ones, keeps the exact top-k,
+// sorted, in cand[0, K), raises the threshold to the k-th, and empties the raw regions. Every
+// consumer thread calls it; `wcnt` is the calling warp's raw count (returned as 0).
 template <int kNT>
-__device__ void raise_threshold(const SampleDev& p, uint64_t* cand, int K, SampleShared* sh) {
-    if (K < p.k) return;
-    uint32_t mn = 0xffffffffu;
-    for (int i = threadIdx.x; i < K; i += kNT) {
-        const uint32_t hi = static_cast<uint32_t>(cand[i] >> 32);
-        mn = hi < mn ? hi : mn;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const uint32_t o = __shfl_xor_sync(0xffffffffu, mn, off);
-        mn = o < mn ? o : mn;
-    }
-    if (threadIdx.x == 0) sh->min_key_hi = 0xffffffffu;
+__device__ void prune(const SampleDev& p, uint64_t* cand, const uint2* raw, int& wcnt, SampleShared* sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) sh->wcnt[warp] = wcnt;
     group_sync<kNT>();
-    if ((threadIdx.x & 31) == 0) atomicMin(&sh->min_key_hi, mn);
+    int off = sh->K, n = sh->K;
+    for (int w = 0; w < kSampWarps; ++w) {
+        if (w < warp) off += sh->wcnt[w];
+        n += sh->wcnt[w];
+    }
+    const uint2* mine = raw + warp * kRawPerWarp;
+    for (int j = lane; j < wcnt; j += 32) {
+        const uint2 e = mine[j];
+        cand[off + j] = loom_rank_key(tempered(__uint_as_float(e.x), p.T, p.greedy), static_cast<int32_t>(e.y));
+    }
     group_sync<kNT>();
+    const int K = topk_select_sorted<kNT, kCandCap>(cand, n, p.k, &sh->tk);
     if (threadIdx.x == 0) {
-        const float t = order_key_to_float(sh->min_key_hi);
-        if (t > sh->thr_y) {
-            sh->thr_y = t;
-            sh->X = inverse_threshold(t, p.T, p.greedy);
+        sh->K = K;
+        sh->fail = 0;
+        if (K == p.k) {
+            const float t = rank_key_value(cand[K - 1]);
+            if (t > sh->thr_y) {
+                sh->thr_y = t;
+                sh->X = inverse_threshold(t, p.T, p.greedy);
+            }
         }
     }
+    wcnt = 0;
     group_sync<kNT>();
 }
 
-// Sorts the K (<= k) kept keys of a whole row, fills up to k with NaN ids when the row has fewer
-// than k non-NaN values, and emits the row's result (a decision, or a shard record).
+// The K (<= k) best keys of a whole row, sorted: fill up to k with NaN ids when the row has fewer
+// than k non-NaN values, then emit the row's result (a decision, or a shard record).
 template <int kDtype, int kNT>
-__device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t row, uint64_t* cand, int K, LseAcc lse,
-                             bool bad, SampleShared* sh) {
+__device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t row, uint64_t* cand, double* S, int K,
+                             LseAcc lse, bool bad, SampleShared* sh) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     const unsigned char* rowp = g.base + row * g.row_stride * kEsz;
@@ -171,7 +214,7 @@ __device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t ro
     }
     const int kk = static_cast<int>(p.k < g.width ? p.k : g.width); // a shard may be narrower than k
     if (K < kk) {
-        // NaN fill in column order: NaN ranks below everything, lower id first
+        // NaN fill in column order: NaN ranks below everything, lower id first (after the sorted K)
         if (tid == 0) sh->nan_have = K;
         group_sync<kNT>();
         for (int64_t base = 0; base < g.width; base += kNT) {
@@ -201,8 +244,6 @@ __device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t ro
         }
         K = kk;
     }
-    const int P = next_pow2(K);
-    topk_sort_desc<kNT>(cand, K, P);
     if (p.shard) {
         unsigned char* rec = p.shard_out + row * p.rec_bytes;
         if (tid == 0) {
@@ -221,8 +262,7 @@ __device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t ro
         return;
     }
     if (warp == 0) {
-        double* e = reinterpret_cast<double*>(cand + kDecideOffset);
-        double* S = e + kDecideOffset;
+        double* e = reinterpret_cast<double*>(cand + kDecideSlots);
         if (p.greedy) {
             if (lane == 0) {
                 const float x0 = load_global_elem<kDtype>(rowp, 0);
@@ -262,9 +302,11 @@ struct SampleOp {
     const SampleDev& p;
     SampleShared* sh;
     uint64_t* cand;
-    uint32_t* bitmap;
-    int32_t* pen;
+    uint2* raw;     // [kSampWarps][kRawPerWarp] raw candidates (value bits, global id)
+    int32_t* hset;  // history hash set of the segment
+    double* S;      // decision scratch
     LseAcc lse;
+    int wcnt;       // this warp's raw candidates (identical in its lanes)
     bool first_chunk;
 
     __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
@@ -273,80 +315,77 @@ struct SampleOp {
     __device__ void begin_segment(const Segment& s) {
         const int tid = threadIdx.x;
         if (tid == 0) {
-            sh->cnt = 0;
-            sh->fail = 0x7fffffff;
+            sh->K = 0;
+            sh->fail = 0;
             sh->bad = 0;
             sh->X = neg_inf();
             sh->thr_y = neg_inf();
             sh->warm_key = 0xffffffffu;
         }
         lse = lse_init();
+        wcnt = 0;
         first_chunk = true;
+        if (p.penalty)
+            for (int i = tid; i < kHashSlots; i += kNT) hset[i] = -1;
         group_sync<kNT>();
-        if (p.hist_len > 0) {
-            const int32_t* h = row_hist(s.row);
-            for (int j = tid; j < p.hist_len; j += kNT) {
-                const int32_t id = __ldg(h + j);
-                if (id < 0 || id >= p.vocab_limit) sh->bad = 1;
+        // Validate the whole history. Each distinct id inside this segment joins the set and is
+        // inserted once with its penalised, tempered value (read from global memory).
+        const int64_t seg_lo = p.vocab_offset + s.j0, seg_hi = p.vocab_offset + s.j1;
+        for (int j = tid; j < p.hist_len; j += kNT) {
+            const int32_t id = __ldg(row_hist(s.row) + j);
+            if (id < 0 || id >= p.vocab_limit) {
+                sh->bad = 1;
+            } else if (p.penalty && id >= seg_lo && id < seg_hi && hash_insert(hset, id)) {
+                const float x = load_global_elem<kDtype>(row_ptr(s.row), id - p.vocab_offset);
+                const float y = tempered(penalise(x, p.r), p.T, p.greedy);
+                if (p.lse) lse_offer(lse, y);
+                if (y == y) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, id);
             }
         }
+        group_sync<kNT>();
+        // edges: the few elements outside the 16-byte-aligned interior (history ids are in already)
         const int32_t n_edges = segment_edge_count(s, kEsz);
         if (tid < n_edges) {
             const int64_t col = segment_edge_col(s, kEsz, tid);
-            float x = load_global_elem<kDtype>(row_ptr(s.row), col);
-            const int64_t gid = p.vocab_offset + col;
-            if (p.penalty) {
-                const int32_t* h = row_hist(s.row);
-                bool in = false;
-                for (int j = 0; j < p.hist_len && !in; ++j) in = (__ldg(h + j) == gid);
-                if (in) x = penalise(x, p.r);
+            const int32_t gid = static_cast<int32_t>(p.vocab_offset + col);
+            if (!(p.penalty && hash_contains(hset, gid))) {
+                const float y = tempered(load_global_elem<kDtype>(row_ptr(s.row), col), p.T, p.greedy);
+                if (p.lse) lse_offer(lse, y);
+                if (y == y) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, gid);
             }
-            const float y = tempered(x, p.T, p.greedy);
-            if (p.lse) lse_offer(lse, y);
-            if (y == y) cand[atomicAdd(&sh->cnt, 1)] = loom_rank_key(y, static_cast<int32_t>(gid));
         }
         group_sync<kNT>();
         if (tid == 0 && sh->bad) record_status(p.status, LOOM_SELECT_EHISTORY);
+        if (sh->K > p.k + kPruneSlack) prune<kNT>(p, cand, raw, wcnt, sh);
+    }
+
+    __device__ __forceinline__ bool is_history(int64_t gid) const {
+        return p.penalty && hash_contains(hset, static_cast<int32_t>(gid));
     }
 
     __device__ void chunk(const Segment& s, const unsigned char* data, int64_t col0, int32_t n) {
-        const int tid = threadIdx.x, lane = tid & 31;
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
         const int32_t nvec = n / kPer;
         const uint4* v4 = reinterpret_cast<const uint4*>(data);
         const int64_t gid0 = p.vocab_offset + col0;
-        const bool use_pen = p.penalty;
 
-        // 1. history ids inside this stage: mark them, list each distinct one once
-        if (use_pen) {
-            const int32_t nwords = (n + 31) >> 5;
-            for (int w = tid; w < nwords; w += kNT) bitmap[w] = 0u;
-            if (tid == 0) sh->pen_cnt = 0;
-            group_sync<kNT>();
-            const int32_t* h = row_hist(s.row);
-            for (int j = tid; j < p.hist_len; j += kNT) {
-                const int64_t c = static_cast<int64_t>(__ldg(h + j)) - gid0;
-                if (c >= 0 && c < n) {
-                    const uint32_t bit = 1u << (c & 31);
-                    const uint32_t old = atomicOr(&bitmap[c >> 5], bit);
-                    if (!(old & bit)) pen[atomicAdd(&sh->pen_cnt, 1)] = static_cast<int32_t>(c);
-                }
-            }
-            group_sync<kNT>();
-        }
-
-        // 2. seed the threshold from the segment's first stage
+        // 1. seed the threshold from the segment's first stage
         if (first_chunk) {
             first_chunk = false;
             float m = neg_inf();
+            int64_t at = -1;
             for (int32_t v = tid; v < nvec; v += kNT) {
                 Vec16<kDtype> e;
                 e.unpack(v4[v]);
-                uint32_t hb = 0;
-                if (use_pen) hb = bitmap[(v * kPer) >> 5] >> ((v * kPer) & 31);
 #pragma unroll
                 for (int q = 0; q < kPer; ++q)
-                    if (!((hb >> q) & 1u)) m = fmaxf(m, e.x[q]);
+                    if (e.x[q] > m) {
+                        m = e.x[q];
+                        at = gid0 + static_cast<int64_t>(v) * kPer + q;
+                    }
             }
+            // a lane whose maximum is a history id vouches for nothing
+            if (at >= 0 && is_history(at)) m = neg_inf();
             const float sorted = warp_sort_desc(m);
             const int q = (p.k + kSampWarps - 1) / kSampWarps;
             const float bw = q <= 32 ? __shfl_sync(0xffffffffu, sorted, q - 1) : neg_inf();
@@ -363,82 +402,91 @@ struct SampleOp {
             group_sync<kNT>();
         }
 
-        // 3. the penalised history entries of this stage
-        if (use_pen) {
-            const int pc = sh->pen_cnt;
-            const float thr = sh->thr_y;
-            for (int j = tid; j < pc; j += kNT) {
-                const int32_t c = pen[j];
-                const float y = tempered(penalise(smem_elem<kDtype>(data, c), p.r), p.T, p.greedy);
-                if (p.lse) lse_offer(lse, y);
-                if (y == y && y >= thr) cand[atomicAdd(&sh->cnt, 1)] = loom_rank_key(y, static_cast<int32_t>(gid0 + c));
-            }
-            // (buffer room: cnt <= kPruneAt before the stage and pc <= kMaxHistory)
-        }
-
-        // 4. the stream: compare against X, append the few that pass; prune and resume when full
-        const int32_t nrows = (nvec + kNT - 1) / kNT;
-        int32_t my_row = 0;
-        for (;;) {
+        // 2. the stream: kStepVecs vectors per thread per step, one vote; passes go raw to the
+        //    warp's region, vector by vector. A vector that does not fit stops the warp (it resumes
+        //    at that vector after the prune, when any one vector fits: 32 * kPer <= kRawPerWarp).
+        uint2* mine = raw + warp * kRawPerWarp;
+        const int32_t nsteps = (nvec + kStepVecs * kNT - 1) / (kStepVecs * kNT);
+        int32_t step = 0, sub = 0;
+        // every round but the last makes progress (a prune, then at least one vector), so this
+        // bound is never reached; it only guarantees that the loop ends
+        const int32_t max_rounds = nsteps * kStepVecs + 2;
+        for (int32_t round = 0;; ++round) {
             const float X = sh->X;
-            for (; my_row < nrows; ++my_row) {
-                const int32_t v = my_row * kNT + tid;
-                const bool valid = v < nvec;
-                Vec16<kDtype> e;
-                uint32_t hb = 0;
-                uint32_t mask = 0;
-                if (valid) {
-                    e.unpack(v4[v]);
-                    if (use_pen) hb = bitmap[(v * kPer) >> 5] >> ((v * kPer) & 31);
+            for (; step < nsteps; ++step, sub = 0) {
+                const int32_t v0 = step * kStepVecs * kNT + tid;
+                Vec16<kDtype> e[kStepVecs];
+                float mu = __int_as_float(0x7fc00000); // NaN: fmaxf skips it
 #pragma unroll
-                    for (int q = 0; q < kPer; ++q)
-                        if (!((hb >> q) & 1u) && e.x[q] >= X) mask |= 1u << q;
+                for (int u = 0; u < kStepVecs; ++u) {
+                    if (v0 + u * kNT < nvec) {
+                        e[u].unpack(v4[v0 + u * kNT]);
+#pragma unroll
+                        for (int q = 0; q < kPer; ++q) mu = fmaxf(mu, e[u].x[q]);
+                    }
                 }
-                if (__any_sync(0xffffffffu, mask != 0u)) {
-                    const int np = __popc(mask);
-                    int incl = np;
+                if (__any_sync(0xffffffffu, mu >= X)) {
+                    bool stopped = false;
 #pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const int o = __shfl_up_sync(0xffffffffu, incl, off);
-                        if (lane >= off) incl += o;
-                    }
-                    const int total = __shfl_sync(0xffffffffu, incl, 31);
-                    int base = 0;
-                    if (lane == 31) base = atomicAdd(&sh->cnt, total);
-                    base = __shfl_sync(0xffffffffu, base, 31);
-                    if (base + total > kCandCap) {
-                        if (lane == 0) atomicMin(&sh->fail, base);
-                        break; // this row again after the prune
-                    }
-                    int pos = base + incl - np;
+                    for (int u = 0; u < kStepVecs; ++u) {
+                        if (u < sub) continue;  // inserted before the prune
+                        const int32_t v = v0 + u * kNT;
+                        uint32_t m = 0;
+                        if (v < nvec && mu >= X) {
 #pragma unroll
-                    for (int q = 0; q < kPer; ++q) {
-                        if ((mask >> q) & 1u) {
-                            const float y = tempered(e.x[q], p.T, p.greedy);
-                            cand[pos++] = loom_rank_key(y, static_cast<int32_t>(gid0 + v * kPer + q));
+                            for (int q = 0; q < kPer; ++q)
+                                if (e[u].x[q] >= X && !is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) m |= 1u << q;
                         }
+                        const int np = __popc(m);
+                        int incl = np;
+#pragma unroll
+                        for (int off = 1; off < 32; off <<= 1) {
+                            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+                            if (lane >= off) incl += o;
+                        }
+                        const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+                        if (wcnt + wtotal > kRawPerWarp) {
+                            if (lane == 0) sh->fail = 1;
+                            sub = u;
+                            stopped = true;
+                            break;
+                        }
+                        int pos = wcnt + incl - np;
+#pragma unroll
+                        for (int q = 0; q < kPer; ++q)
+                            if ((m >> q) & 1u)
+                                mine[pos++] = make_uint2(__float_as_uint(e[u].x[q]),
+                                                         static_cast<uint32_t>(gid0 + static_cast<int64_t>(v) * kPer + q));
+                        wcnt += wtotal;
+                    }
+                    if (stopped) break; // this step again (from vector `sub`) after the prune
+                }
+                if (p.lse) {
+                    // every element once (history ids were offered at the segment start)
+#pragma unroll
+                    for (int u = 0; u < kStepVecs; ++u) {
+                        const int32_t v = v0 + u * kNT;
+                        if (v < nvec)
+#pragma unroll
+                            for (int q = 0; q < kPer; ++q)
+                                if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q))
+                                    lse_offer(lse, tempered(e[u].x[q], p.T, p.greedy));
                     }
                 }
-                if (p.lse && valid) {
-#pragma unroll
-                    for (int q = 0; q < kPer; ++q)
-                        if (!((hb >> q) & 1u)) lse_offer(lse, tempered(e.x[q], p.T, p.greedy));
-                }
             }
+            if (lane == 0) sh->wcnt[warp] = wcnt;
             group_sync<kNT>();
-            const int fail = sh->fail;
-            const int cnt = sh->cnt;
-            const bool finished = fail == 0x7fffffff;
-            if (finished && cnt <= kPruneAt) break;
-            const int held = cnt < fail ? cnt : fail;
+            const bool failed = sh->fail != 0;
+            int held = sh->K;
+            for (int w = 0; w < kSampWarps; ++w) held += sh->wcnt[w];
+            if (!failed && held <= p.k + kPruneSlack) break;
             group_sync<kNT>();
-            const int K = topk_select_compact<kNT, kCandCap / kNT>(cand, held, p.k, &sh->tk);
-            if (threadIdx.x == 0) {
-                sh->cnt = K;
-                sh->fail = 0x7fffffff;
+            prune<kNT>(p, cand, raw, wcnt, sh);
+            if (!failed) break;
+            if (round >= max_rounds) {  // unreachable by construction (see above)
+                if (tid == 0) record_status(p.status, LOOM_SELECT_ETIMEOUT);
+                break;
             }
-            raise_threshold<kNT>(p, cand, K, sh);
-            if (finished) break;
         }
     }
 
@@ -457,13 +505,12 @@ struct SampleOp {
                 for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
             sh->seg_lse = a;
         }
-        group_sync<kNT>();
-        const int cnt = sh->cnt;
-        const int K = topk_select_compact<kNT, kCandCap / kNT>(cand, cnt, p.k, &sh->tk);
+        prune<kNT>(p, cand, raw, wcnt, sh);  // also syncs
+        const int K = sh->K;
         const LseAcc seg = sh->seg_lse;
         const bool bad = sh->bad != 0;
         if (s.count == 1) {
-            finalize_row<kDtype, kNT>(p, g, s.row, cand, K, seg, bad, sh);
+            finalize_row<kDtype, kNT>(p, g, s.row, cand, S, K, seg, bad, sh);
             return;
         }
         // a piece of a split row: write its record, take a ticket, the last one merges
@@ -501,22 +548,21 @@ struct SampleOp {
             part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
             part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
             tot = lse_merge(tot, part);
-            if (have + c > kCandCap) {
-                have = topk_select_compact<kNT, kCandCap / kNT>(cand, have, p.k, &sh->tk);
-            }
+            if (have + c > kCandCap) have = topk_select_sorted<kNT, kCandCap>(cand, have, p.k, &sh->tk);
             const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
             for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
             have += c;
             group_sync<kNT>();
         }
-        const int Kf = topk_select_compact<kNT, kCandCap / kNT>(cand, have, p.k, &sh->tk);
+        const int Kf = topk_select_sorted<kNT, kCandCap>(cand, have, p.k, &sh->tk);
         if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
-        finalize_row<kDtype, kNT>(p, g, s.row, cand, Kf, tot, any_bad, sh);
+        finalize_row<kDtype, kNT>(p, g, s.row, cand, S, Kf, tot, any_bad, sh);
     }
 };
 
 constexpr size_t kSampDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
-                                (kSampStageBytes / 2 / 32) * sizeof(uint32_t) + kMaxHistory * sizeof(int32_t);
+                                kSampWarps * kRawPerWarp * sizeof(uint2) + kHashSlots * sizeof(int32_t) +
+                                kDecideSlots * sizeof(double);
 
 template <int kDtype>
 __global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel(StreamGeom g, SampleDev p) {
@@ -525,9 +571,10 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel
     __shared__ SampleShared sh;
     unsigned char* ring = dyn;
     uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + static_cast<size_t>(kSampStages) * kSampStageBytes);
-    uint32_t* bitmap = reinterpret_cast<uint32_t*>(cand + kCandCap);
-    int32_t* pen = reinterpret_cast<int32_t*>(bitmap + kSampStageBytes / 2 / 32);
-    SampleOp<kDtype> op{g, p, &sh, cand, bitmap, pen, lse_init(), true};
+    uint2* raw = reinterpret_cast<uint2*>(cand + kCandCap);
+    int32_t* hset = reinterpret_cast<int32_t*>(raw + kSampWarps * kRawPerWarp);
+    double* S = reinterpret_cast<double*>(hset + kHashSlots);
+    SampleOp<kDtype> op{g, p, &sh, cand, raw, hset, S, lse_init(), 0, true};
     stream_ranges<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 
@@ -570,11 +617,10 @@ __global__ void __launch_bounds__(kMergeNT) shard_merge_kernel(const unsigned ch
         return;
     }
     int have = 0;
-    const int cap = kCandCap;
     for (int g = 0; g < n_shards; ++g) {
         const unsigned char* rec = records + (static_cast<size_t>(g) * rows + row) * rec_bytes;
         const int32_t c = reinterpret_cast<const RecordHead*>(rec)->count;
-        if (have + c > cap) have = topk_select_compact<kMergeNT, kCandCap / kMergeNT>(mcand, have, k, &tk);
+        if (have + c > kCandCap) have = topk_select_sorted<kMergeNT, kCandCap>(mcand, have, k, &tk);
         const uint2* pairs = reinterpret_cast<const uint2*>(rec + 16);
         for (int i = tid; i < c; i += kMergeNT) {
             const uint2 pr = pairs[i];
@@ -583,11 +629,10 @@ __global__ void __launch_bounds__(kMergeNT) shard_merge_kernel(const unsigned ch
         have += c;
         __syncthreads();
     }
-    const int K = topk_select_compact<kMergeNT, kCandCap / kMergeNT>(mcand, have, k, &tk);
-    topk_sort_desc<kMergeNT>(mcand, K, next_pow2(K));
+    const int K = topk_select_sorted<kMergeNT, kCandCap>(mcand, have, k, &tk);
     if (tid < 32) {
-        double* e = reinterpret_cast<double*>(mcand + kDecideOffset);
-        double* S = e + kDecideOffset;
+        double* e = reinterpret_cast<double*>(mcand + kDecideSlots);
+        double* S = e + kDecideSlots;
         decide_warp(mcand, K, top_p, __ldg(u + row), e, S, &sel_id, &sel_prob, &sel_y);
         if (tid == 0) {
             out_ids[row] = sel_id;

@@ -129,6 +129,54 @@ __device__ void topk_sort_desc(uint64_t* cand, int n, int P) {
     }
 }
 
+// Exact rank selection of small sets: each key's rank is the number of larger keys (keys are
+// distinct), so the K = min(k, n) largest land, sorted descending, at cand[rank] in [0, K).
+// O(n^2 / kNT) compares with broadcast shared-memory reads; n <= kPer * kNT.
+template <int kNT, int kPer>
+__device__ int topk_rank_sort(uint64_t* cand, int n, int k) {
+    const int tid = threadIdx.x;
+    uint64_t mine[kPer];
+    int rank[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = tid + j * kNT;
+        mine[j] = i < n ? cand[i] : 0ull;
+        rank[j] = 0;
+    }
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        const uint64_t o0 = cand[i], o1 = cand[i + 1], o2 = cand[i + 2], o3 = cand[i + 3];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            rank[j] += static_cast<int>(o0 > mine[j]) + static_cast<int>(o1 > mine[j]) + static_cast<int>(o2 > mine[j]) +
+                       static_cast<int>(o3 > mine[j]);
+    }
+    for (; i < n; ++i) {
+        const uint64_t o = cand[i];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) rank[j] += static_cast<int>(o > mine[j]);
+    }
+    group_sync<kNT>();
+    const int K = n < k ? n : k;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i2 = tid + j * kNT;
+        if (i2 < n && rank[j] < K) cand[rank[j]] = mine[j];
+    }
+    group_sync<kNT>();
+    return K;
+}
+
+// The K = min(k, n) largest keys of cand[0, n), sorted descending, in cand[0, K). Large sets are
+// first cut to k by the radix select, then ranked. n <= kCap (the buffer), k <= 1024.
+template <int kNT, int kCap>
+__device__ int topk_select_sorted(uint64_t* cand, int n, int k, TopkShared* sh) {
+    if (n > 2 * kNT) n = topk_select_compact<kNT, kCap / kNT>(cand, n, k, sh);
+    if (n <= kNT) return topk_rank_sort<kNT, 1>(cand, n, k);
+    if (n <= 2 * kNT) return topk_rank_sort<kNT, 2>(cand, n, k);
+    return topk_rank_sort<kNT, (1024 + kNT - 1) / kNT>(cand, n, k);
+}
+
 __device__ __forceinline__ int next_pow2(int n) {
     int p = 1;
     while (p < n) p <<= 1;

@@ -102,11 +102,18 @@ static void gpu_checks() {
     float* ds = upload(s);
     const std::vector<float> u = {0.5f, 0.25f};
     float* du = upload(u);
-    const std::vector<int32_t> hist = {5, 5};  // row 0: id 5 penalised (7 -> 7/2); row 1: id 5 as well
+    // row 0 [0.1, 2, -1, 2] with id 1 penalised by 2 (2 -> 1): argmax 3
+    // row 1 [0.5, 7, 1, 7]  with id 3 penalised by 2 (7 -> 3.5): argmax 1
+    const std::vector<int32_t> hist = {1, 3};
     int32_t* dh = upload(hist);
     loom_sample_params p{1.0f, 2.0f, 1, 1.0f};
     const SampleResult r = sample_rows(ds, 2, 4, 4, dh, 1, du, p);
-    CHECK((r.ids == std::vector<int32_t>{1, 3}));  // row 1 is ids 4..7: [0.5, 7/2, 1, 7] -> 3
+    CHECK((r.ids == std::vector<int32_t>{3, 1}));
+    // a history id outside the vocabulary is a loom::Error
+    const std::vector<int32_t> bad = {4, 0};
+    int32_t* db = upload(bad);
+    CHECK_THROWS(sample_rows(ds, 2, 4, 4, db, 1, du, p), "outside the vocabulary");
+    cudaFree(db);
     CHECK(r.probs.size() == 2 && r.probs[0] == 1.0f && r.probs[1] == 1.0f);
     for (void* p_ : {static_cast<void*>(d1), static_cast<void*>(d2), static_cast<void*>(d3), static_cast<void*>(da),
                      static_cast<void*>(dw), static_cast<void*>(ds), static_cast<void*>(du), static_cast<void*>(dh)})
