@@ -31,7 +31,7 @@ struct ArgmaxOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     static constexpr int kPer = 16 / kEsz;
     static constexpr int kU = 4; // vectors per thread per step
-    const StreamGeom& g;
+    StreamGeom g;  // copies: no pointer into the kernel's parameters
     int64_t lo;
     int32_t* out_ids;
     ArgRecord* records;

@@ -1,11 +1,12 @@
 // select_sample.cu -- the fused sampling chain (K2) and the vocabulary-shard merge (K4).
 //
 // One pass over the logits: rows stream through shared memory (select_stream.cuh). The per-element
-// work is a compare: every thread takes 4 vectors of 16 bytes per step, and one warp vote asks
-// whether any maximum reaches a threshold X. X is exact -- the smallest raw value whose tempered
-// value x / T reaches the current k-th best tempered value -- so every element below it is strictly
-// worse than k elements already kept. The rare elements that pass go, raw, into their warp's own
-// region of shared memory (offsets from ballots, a register counter: no atomics, no divides).
+// work is a compare without branches: each thread marks, in a register bitmask, which of its
+// vectors of the stage (16 bytes each) have a maximum reaching a threshold X. Every element below X
+// is strictly worse than k elements already kept (X is at most the smallest raw value whose tempered
+// value x / T reaches the current k-th best). At the end of the stage each thread sweeps its few
+// marked vectors: the elements that pass go, raw, into the thread's own slots in shared memory (one
+// store each; no atomics, no shuffles, no divides).
 //
 // At the end of a stage, when more than k + kPruneSlack candidates are held, they are tempered with
 // an IEEE divide (in parallel), the exact top-k is kept as 64-bit rank keys, and X rises to the k-th.
@@ -13,8 +14,8 @@
 // the warps' ceil(k / warps)-th largest is a value that at least k elements reach.
 //
 // The repetition penalty touches only the history ids: at the start of a row segment the distinct
-// ones inside it go into a shared-memory hash set and are inserted once, with their penalised,
-// tempered values read from global memory; the stream skips set members (looked up only for
+// ones inside it go into a shared-memory hash set and a list. Each stage inserts the listed ids it
+// holds with their penalised, tempered values; the stream skips set members (looked up only for
 // elements that pass X). So the per-element path carries no penalty work.
 //
 // At the end of a row the exact top-k is ranked into order and the survivor decision runs in double
@@ -34,17 +35,16 @@ constexpr int kSampNT = kSampWarps * 32;
 constexpr int kSampStages = 4;
 constexpr int kSampStageBytes = 32768;
 constexpr int kCandCap = 4096;    // candidate rank keys in shared memory
-constexpr int kRawPerWarp = 256;  // raw candidates a warp holds between prunes
+constexpr int kSlots = 8;         // raw candidates a thread holds between prunes
 constexpr int kPruneSlack = 64;   // prune at a stage end when more than k + this many are held
 constexpr int kHashSlots = 4096;  // history hash set (load <= 1/2 at kMaxHistory ids)
 constexpr int kDecideSlots = 1024;
-constexpr int kStepVecs = 4;      // vectors per thread per step of the stream
-static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kSampWarps * kRawPerWarp, "a prune's keys must fit");
-static_assert(kCandCap >= kMaxHistory + 16, "a segment's penalised entries and edges must fit");
+static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kMaxHistory, "penalised entries of a stage must fit");
+static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kSampNT * kSlots, "a prune's keys must fit");
 static_assert(LOOM_SELECT_MAX_TOP_K <= kDecideSlots && 2 * kDecideSlots <= kCandCap,
               "decision scratch e[] lives in key slots [1024, 2048)");
 static_assert(2 * kMaxHistory <= kHashSlots, "hash set load");
-static_assert(kRawPerWarp >= 32 * 8, "one vector's passes (32 lanes x 8 bf16) must fit an empty warp region");
+static_assert(kSlots >= 8, "one vector's passes (8 bf16) must fit a thread's empty slots");
 
 struct SampleDev {
     float T, r, p;
@@ -75,8 +75,9 @@ struct RecordHead {
 struct SampleShared {
     TopkShared tk;
     int K;         // rank keys held in cand[0, K)
-    int fail;      // a warp's raw region filled up mid-stage
+    int fail;      // a thread's slots filled up mid-stage
     int bad;
+    int n_uniq;
     uint32_t warm_key;
     float X;
     float thr_y;
@@ -148,45 +149,49 @@ __device__ __forceinline__ bool hash_insert(int32_t* set, int32_t id) {
     return false;
 }
 
-// Tempers every warp's raw candidates into rank keys after the held ones, keeps the exact top-k,
-// sorted, in cand[0, K), raises the threshold to the k-th, and empties the raw regions. Every
-// consumer thread calls it; `wcnt` is the calling warp's raw count (returned as 0).
+// Tempers every thread's raw candidates into rank keys after the held ones, keeps the exact top-k,
+// sorted, in cand[0, K), raises the threshold to the k-th, and empties the slots. Every consumer
+// thread calls it with its own slot count `qn` (returned as 0).
 template <int kNT>
-__device__ void prune(const SampleDev& p, uint64_t* cand, const uint2* raw, int& wcnt, SampleShared* sh) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) sh->wcnt[warp] = wcnt;
-    group_sync<kNT>();
-    int off = sh->K, n = sh->K;
-    for (int w = 0; w < kSampWarps; ++w) {
-        if (w < warp) off += sh->wcnt[w];
-        n += sh->wcnt[w];
+__device__ void prune(const SampleDev p, uint64_t* cand, const uint2* slots, int& qn, SampleShared* sh) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    int excl = qn;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, excl, off);
+        if (lane >= off) excl += o;
     }
-    const uint2* mine = raw + warp * kRawPerWarp;
-    for (int j = lane; j < wcnt; j += 32) {
-        const uint2 e = mine[j];
-        cand[off + j] = loom_rank_key(tempered(__uint_as_float(e.x), p.T, p.greedy), static_cast<int32_t>(e.y));
+    const int wsum = __shfl_sync(0xffffffffu, excl, 31);
+    excl -= qn;
+    int base = 0;
+    if (lane == 0) base = atomicAdd(&sh->K, wsum);
+    base = __shfl_sync(0xffffffffu, base, 0);
+    for (int j = 0; j < qn; ++j) {
+        const uint2 e = slots[j * kNT + tid];
+        cand[base + excl + j] = loom_rank_key(tempered(__uint_as_float(e.x), p.T, p.greedy), static_cast<int32_t>(e.y));
     }
+    qn = 0;
     group_sync<kNT>();
+    const int n = sh->K;
     const int K = topk_select_sorted<kNT, kCandCap>(cand, n, p.k, &sh->tk);
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         sh->K = K;
         sh->fail = 0;
         if (K == p.k) {
             const float t = rank_key_value(cand[K - 1]);
             if (t > sh->thr_y) {
                 sh->thr_y = t;
-                sh->X = inverse_threshold(t, p.T, p.greedy);
+                sh->X = inverse_threshold_bound(t, p.T, p.greedy);
             }
         }
     }
-    wcnt = 0;
     group_sync<kNT>();
 }
 
 // The K (<= k) best keys of a whole row, sorted: fill up to k with NaN ids when the row has fewer
 // than k non-NaN values, then emit the row's result (a decision, or a shard record).
 template <int kDtype, int kNT>
-__device__ void finalize_row(const SampleDev& p, const StreamGeom& g, int64_t row, uint64_t* cand, double* S, int K,
+__device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row, uint64_t* cand, double* S, int K,
                              LseAcc lse, bool bad, SampleShared* sh) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
@@ -298,19 +303,24 @@ struct SampleOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     static constexpr int kPer = 16 / kEsz;
     static constexpr int kNT = kSampNT;
-    const StreamGeom& g;
-    const SampleDev& p;
+    StreamGeom g;  // copies: no pointer into the kernel's parameters
+    SampleDev p;
     SampleShared* sh;
     uint64_t* cand;
-    uint2* raw;     // [kSampWarps][kRawPerWarp] raw candidates (value bits, global id)
+    uint2* slots;   // [kSlots][kNT]: thread t's raw candidates (value bits, global id) at [j][t]
     int32_t* hset;  // history hash set of the segment
+    int32_t* uniq;  // its distinct ids, as a list
     double* S;      // decision scratch
     LseAcc lse;
-    int wcnt;       // this warp's raw candidates (identical in its lanes)
+    int qn;         // this thread's raw candidates
     bool first_chunk;
 
     __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
     __device__ const int32_t* row_hist(int64_t row) const { return p.hist + row * static_cast<int64_t>(p.hist_len); }
+
+    __device__ __forceinline__ bool is_history(int64_t gid) const {
+        return p.penalty && hash_contains(hset, static_cast<int32_t>(gid));
+    }
 
     __device__ void begin_segment(const Segment& s) {
         const int tid = threadIdx.x;
@@ -318,49 +328,41 @@ struct SampleOp {
             sh->K = 0;
             sh->fail = 0;
             sh->bad = 0;
+            sh->n_uniq = 0;
             sh->X = neg_inf();
             sh->thr_y = neg_inf();
             sh->warm_key = 0xffffffffu;
         }
         lse = lse_init();
-        wcnt = 0;
+        qn = 0;
         first_chunk = true;
-        if (p.penalty)
-            for (int i = tid; i < kHashSlots; i += kNT) hset[i] = -1;
+        if (p.penalty) {
+            int4* h4 = reinterpret_cast<int4*>(hset);
+            for (int i = tid; i < kHashSlots / 4; i += kNT) h4[i] = make_int4(-1, -1, -1, -1);
+        }
         group_sync<kNT>();
-        // Validate the whole history. Each distinct id inside this segment joins the set and is
-        // inserted once with its penalised, tempered value (read from global memory).
+        // validate the whole history; the distinct ids inside this segment go into the set and list
         const int64_t seg_lo = p.vocab_offset + s.j0, seg_hi = p.vocab_offset + s.j1;
         for (int j = tid; j < p.hist_len; j += kNT) {
             const int32_t id = __ldg(row_hist(s.row) + j);
-            if (id < 0 || id >= p.vocab_limit) {
-                sh->bad = 1;
-            } else if (p.penalty && id >= seg_lo && id < seg_hi && hash_insert(hset, id)) {
-                const float x = load_global_elem<kDtype>(row_ptr(s.row), id - p.vocab_offset);
-                const float y = tempered(penalise(x, p.r), p.T, p.greedy);
-                if (p.lse) lse_offer(lse, y);
-                if (y == y) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, id);
-            }
+            if (id < 0 || id >= p.vocab_limit) sh->bad = 1;
+            else if (p.penalty && id >= seg_lo && id < seg_hi && hash_insert(hset, id))
+                uniq[atomicAdd(&sh->n_uniq, 1)] = id;
         }
         group_sync<kNT>();
-        // edges: the few elements outside the 16-byte-aligned interior (history ids are in already)
+        // edges: the few elements outside the 16-byte-aligned interior, read from global memory
         const int32_t n_edges = segment_edge_count(s, kEsz);
         if (tid < n_edges) {
             const int64_t col = segment_edge_col(s, kEsz, tid);
+            float x = load_global_elem<kDtype>(row_ptr(s.row), col);
             const int32_t gid = static_cast<int32_t>(p.vocab_offset + col);
-            if (!(p.penalty && hash_contains(hset, gid))) {
-                const float y = tempered(load_global_elem<kDtype>(row_ptr(s.row), col), p.T, p.greedy);
-                if (p.lse) lse_offer(lse, y);
-                if (y == y) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, gid);
-            }
+            if (is_history(gid)) x = penalise(x, p.r);
+            const float y = tempered(x, p.T, p.greedy);
+            if (p.lse) lse_offer(lse, y);
+            if (y == y) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, gid);
         }
         group_sync<kNT>();
         if (tid == 0 && sh->bad) record_status(p.status, LOOM_SELECT_EHISTORY);
-        if (sh->K > p.k + kPruneSlack) prune<kNT>(p, cand, raw, wcnt, sh);
-    }
-
-    __device__ __forceinline__ bool is_history(int64_t gid) const {
-        return p.penalty && hash_contains(hset, static_cast<int32_t>(gid));
     }
 
     __device__ void chunk(const Segment& s, const unsigned char* data, int64_t col0, int32_t n) {
@@ -369,7 +371,29 @@ struct SampleOp {
         const uint4* v4 = reinterpret_cast<const uint4*>(data);
         const int64_t gid0 = p.vocab_offset + col0;
 
-        // 1. seed the threshold from the segment's first stage
+        // 1. the history ids this stage holds, with their penalised, tempered values
+        if (p.penalty) {
+            const int nu = sh->n_uniq;
+            const float thr = sh->thr_y;
+            for (int j = tid; j < nu; j += kNT) {
+                const int64_t c = static_cast<int64_t>(uniq[j]) - gid0;
+                if (c < 0 || c >= n) continue;
+                const float y = tempered(penalise(smem_elem<kDtype>(data, static_cast<int32_t>(c)), p.r), p.T, p.greedy);
+                if (p.lse) lse_offer(lse, y);
+                if (y == y && y >= thr) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, static_cast<int32_t>(gid0 + c));
+            }
+            // Room: K <= k + kPruneSlack before the stage, plus nu here, plus every thread's full
+            // slots at the prune. Only very long histories with a large k can overflow: then the
+            // held keys are pruned right away.
+            if (p.k + kPruneSlack + nu + kSampNT * kSlots > kCandCap) {
+                group_sync<kNT>();
+                const bool need = sh->K > p.k + kPruneSlack;
+                group_sync<kNT>();  // every thread has read K before prune() changes it
+                if (need) prune<kNT>(p, cand, slots, qn, sh);
+            }
+        }
+
+        // 2. seed the threshold from the segment's first stage
         if (first_chunk) {
             first_chunk = false;
             float m = neg_inf();
@@ -396,94 +420,79 @@ struct SampleOp {
                 const float ty = tempered(tx, p.T, p.greedy);
                 if (ty > sh->thr_y) {
                     sh->thr_y = ty;
-                    sh->X = inverse_threshold(ty, p.T, p.greedy);
+                    sh->X = inverse_threshold_bound(ty, p.T, p.greedy);
                 }
             }
             group_sync<kNT>();
         }
 
-        // 2. the stream: kStepVecs vectors per thread per step, one vote; passes go raw to the
-        //    warp's region, vector by vector. A vector that does not fit stops the warp (it resumes
-        //    at that vector after the prune, when any one vector fits: 32 * kPer <= kRawPerWarp).
-        uint2* mine = raw + warp * kRawPerWarp;
-        const int32_t nsteps = (nvec + kStepVecs * kNT - 1) / (kStepVecs * kNT);
-        int32_t step = 0, sub = 0;
-        // every round but the last makes progress (a prune, then at least one vector), so this
-        // bound is never reached; it only guarantees that the loop ends
-        const int32_t max_rounds = nsteps * kStepVecs + 2;
-        for (int32_t round = 0;; ++round) {
+        // 3. mark: the vectors whose maximum reaches X (all loads in flight at once, no branches)
+        constexpr int kVecsPerThread = kSampStageBytes / 16 / kNT;
+        static_assert(kVecsPerThread <= 32, "marks are one 32-bit word");
+        uint32_t hits = 0;
+        {
             const float X = sh->X;
-            for (; step < nsteps; ++step, sub = 0) {
-                const int32_t v0 = step * kStepVecs * kNT + tid;
-                Vec16<kDtype> e[kStepVecs];
-                float mu = __int_as_float(0x7fc00000); // NaN: fmaxf skips it
 #pragma unroll
-                for (int u = 0; u < kStepVecs; ++u) {
-                    if (v0 + u * kNT < nvec) {
-                        e[u].unpack(v4[v0 + u * kNT]);
+            for (int i = 0; i < kVecsPerThread; ++i) {
+                const int32_t v = i * kNT + tid;
+                if (v < nvec) {
+                    Vec16<kDtype> e;
+                    e.unpack(v4[v]);
+                    float mu = e.x[0];
 #pragma unroll
-                        for (int q = 0; q < kPer; ++q) mu = fmaxf(mu, e[u].x[q]);
-                    }
-                }
-                if (__any_sync(0xffffffffu, mu >= X)) {
-                    bool stopped = false;
-#pragma unroll
-                    for (int u = 0; u < kStepVecs; ++u) {
-                        if (u < sub) continue;  // inserted before the prune
-                        const int32_t v = v0 + u * kNT;
-                        uint32_t m = 0;
-                        if (v < nvec && mu >= X) {
-#pragma unroll
-                            for (int q = 0; q < kPer; ++q)
-                                if (e[u].x[q] >= X && !is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) m |= 1u << q;
-                        }
-                        const int np = __popc(m);
-                        int incl = np;
-#pragma unroll
-                        for (int off = 1; off < 32; off <<= 1) {
-                            const int o = __shfl_up_sync(0xffffffffu, incl, off);
-                            if (lane >= off) incl += o;
-                        }
-                        const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-                        if (wcnt + wtotal > kRawPerWarp) {
-                            if (lane == 0) sh->fail = 1;
-                            sub = u;
-                            stopped = true;
-                            break;
-                        }
-                        int pos = wcnt + incl - np;
+                    for (int q = 1; q < kPer; ++q) mu = fmaxf(mu, e.x[q]);
+                    hits |= static_cast<uint32_t>(mu >= X) << i;
+                    if (p.lse) {
+                        // every element once (history ids are offered in step 1)
 #pragma unroll
                         for (int q = 0; q < kPer; ++q)
-                            if ((m >> q) & 1u)
-                                mine[pos++] = make_uint2(__float_as_uint(e[u].x[q]),
-                                                         static_cast<uint32_t>(gid0 + static_cast<int64_t>(v) * kPer + q));
-                        wcnt += wtotal;
-                    }
-                    if (stopped) break; // this step again (from vector `sub`) after the prune
-                }
-                if (p.lse) {
-                    // every element once (history ids were offered at the segment start)
-#pragma unroll
-                    for (int u = 0; u < kStepVecs; ++u) {
-                        const int32_t v = v0 + u * kNT;
-                        if (v < nvec)
-#pragma unroll
-                            for (int q = 0; q < kPer; ++q)
-                                if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q))
-                                    lse_offer(lse, tempered(e[u].x[q], p.T, p.greedy));
+                            if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q))
+                                lse_offer(lse, tempered(e.x[q], p.T, p.greedy));
                     }
                 }
             }
-            if (lane == 0) sh->wcnt[warp] = wcnt;
+        }
+
+        // 4. sweep: each thread moves the passing elements of its marked vectors into its slots. A
+        //    thread whose slots cannot take a vector stops there (its marks stay) and, after the
+        //    prune, goes on (any one vector fits empty slots: kPer <= kSlots).
+        // Every round but the last sweeps at least one vector per stopped thread, so the bound is
+        // never reached; it only guarantees that the loop ends.
+        for (int32_t round = 0;; ++round) {
+            const float X = sh->X;  // rises at a prune
+            bool stopped = false;
+            while (hits) {
+                const int i = __ffs(hits) - 1;
+                const int32_t v = i * kNT + tid;
+                Vec16<kDtype> e;
+                e.unpack(v4[v]);
+                const int64_t gv = gid0 + static_cast<int64_t>(v) * kPer;
+                uint32_t m = 0;
+#pragma unroll
+                for (int q = 0; q < kPer; ++q)
+                    if (e.x[q] >= X && !is_history(gv + q)) m |= 1u << q;
+                if (qn + __popc(m) > kSlots) {
+                    stopped = true;
+                    break;
+                }
+#pragma unroll
+                for (int q = 0; q < kPer; ++q)
+                    if ((m >> q) & 1u)
+                        slots[(qn++) * kNT + tid] = make_uint2(__float_as_uint(e.x[q]), static_cast<uint32_t>(gv + q));
+                hits &= hits - 1u;
+            }
+            if (stopped) sh->fail = 1;
+            const int wsum = __reduce_add_sync(0xffffffffu, qn);
+            if (lane == 0) sh->wcnt[warp] = wsum;
             group_sync<kNT>();
             const bool failed = sh->fail != 0;
             int held = sh->K;
             for (int w = 0; w < kSampWarps; ++w) held += sh->wcnt[w];
             if (!failed && held <= p.k + kPruneSlack) break;
             group_sync<kNT>();
-            prune<kNT>(p, cand, raw, wcnt, sh);
+            prune<kNT>(p, cand, slots, qn, sh);
             if (!failed) break;
-            if (round >= max_rounds) {  // unreachable by construction (see above)
+            if (round > kVecsPerThread + 1) {  // unreachable by construction (see above)
                 if (tid == 0) record_status(p.status, LOOM_SELECT_ETIMEOUT);
                 break;
             }
@@ -505,7 +514,7 @@ struct SampleOp {
                 for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
             sh->seg_lse = a;
         }
-        prune<kNT>(p, cand, raw, wcnt, sh);  // also syncs
+        prune<kNT>(p, cand, slots, qn, sh);  // also syncs
         const int K = sh->K;
         const LseAcc seg = sh->seg_lse;
         const bool bad = sh->bad != 0;
@@ -561,8 +570,8 @@ struct SampleOp {
 };
 
 constexpr size_t kSampDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
-                                kSampWarps * kRawPerWarp * sizeof(uint2) + kHashSlots * sizeof(int32_t) +
-                                kDecideSlots * sizeof(double);
+                                kSlots * kSampNT * sizeof(uint2) + kHashSlots * sizeof(int32_t) +
+                                kMaxHistory * sizeof(int32_t) + kDecideSlots * sizeof(double);
 
 template <int kDtype>
 __global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel(StreamGeom g, SampleDev p) {
@@ -571,10 +580,11 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel
     __shared__ SampleShared sh;
     unsigned char* ring = dyn;
     uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + static_cast<size_t>(kSampStages) * kSampStageBytes);
-    uint2* raw = reinterpret_cast<uint2*>(cand + kCandCap);
-    int32_t* hset = reinterpret_cast<int32_t*>(raw + kSampWarps * kRawPerWarp);
-    double* S = reinterpret_cast<double*>(hset + kHashSlots);
-    SampleOp<kDtype> op{g, p, &sh, cand, raw, hset, S, lse_init(), 0, true};
+    uint2* slots = reinterpret_cast<uint2*>(cand + kCandCap);
+    int32_t* hset = reinterpret_cast<int32_t*>(slots + kSlots * kSampNT);
+    int32_t* uniq = hset + kHashSlots;
+    double* S = reinterpret_cast<double*>(uniq + kMaxHistory);
+    SampleOp<kDtype> op{g, p, &sh, cand, slots, hset, uniq, S, lse_init(), 0, true};
     stream_ranges<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 

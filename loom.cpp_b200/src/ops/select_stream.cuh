@@ -123,7 +123,7 @@ struct StreamCtl {
 //   op.end_chunk(seg)                          after the chunk, before its stage is released
 //   op.end_segment(seg)                        after the segment's last chunk
 template <int kStages, int kStageBytes, int kConsumerWarps, class Op>
-__device__ void stream_ranges(const StreamGeom& g, Op& op, unsigned char* ring, StreamCtl* ctl, int* status) {
+__device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, StreamCtl* ctl, int* status) {
     static_assert(kStages <= 16, "ring too deep");
     static_assert(kStageBytes % 16 == 0, "stage must be a multiple of 16 bytes");
     constexpr int kConsumers = kConsumerWarps * 32;

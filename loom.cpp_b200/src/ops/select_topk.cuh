@@ -144,14 +144,15 @@ __device__ int topk_rank_sort(uint64_t* cand, int n, int k) {
         rank[j] = 0;
     }
     int i = 0;
-    for (; i + 4 <= n; i += 4) {
+    const int my_n = tid < n ? n : 0;  // threads that own no key skip the count
+    for (; i + 4 <= my_n; i += 4) {
         const uint64_t o0 = cand[i], o1 = cand[i + 1], o2 = cand[i + 2], o3 = cand[i + 3];
 #pragma unroll
         for (int j = 0; j < kPer; ++j)
             rank[j] += static_cast<int>(o0 > mine[j]) + static_cast<int>(o1 > mine[j]) + static_cast<int>(o2 > mine[j]) +
                        static_cast<int>(o3 > mine[j]);
     }
-    for (; i < n; ++i) {
+    for (; i < my_n; ++i) {
         const uint64_t o = cand[i];
 #pragma unroll
         for (int j = 0; j < kPer; ++j) rank[j] += static_cast<int>(o > mine[j]);
@@ -191,6 +192,26 @@ __device__ __forceinline__ int32_t float_to_ordinal(float x) {
 __device__ __forceinline__ float ordinal_to_float(int32_t k) { return __int_as_float(k < 0 ? (k ^ 0x7fffffff) : k); }
 
 __device__ __forceinline__ float tempered(float x, float T, bool greedy) { return greedy ? x : __fdiv_rn(x, T); }
+
+// A float X with tempered(x) < t for every x < X (t not NaN): X is at most the exact inverse
+// computed below, so filtering on x >= X drops only elements that tempered(x) < t rules out. It
+// starts a few ulps under t * T and checks that tempered(X) < t (then X lies below the exact
+// boundary by monotonicity); one or two divides instead of a search.
+__device__ float inverse_threshold(float t, float T, bool greedy);
+
+__device__ __forceinline__ float inverse_threshold_bound(float t, float T, bool greedy) {
+    if (greedy || t == -__int_as_float(0x7f800000)) return t;
+    const float guess = __fmul_rn(t, T);
+    if (guess == guess && guess != __int_as_float(0x7f800000) && guess != -__int_as_float(0x7f800000)) {
+        int64_t o = float_to_ordinal(guess) - 4;
+        for (int i = 0; i < 8; ++i, o -= 8) {
+            if (o <= float_to_ordinal(-__int_as_float(0x7f800000))) break;
+            const float x = ordinal_to_float(static_cast<int32_t>(o));
+            if (tempered(x, T, false) < t) return x;  // every x' <= x has tempered(x') < t too
+        }
+    }
+    return inverse_threshold(t, T, greedy);
+}
 
 // The smallest float x with tempered(x) >= t (t not NaN): every x below it has tempered(x) < t.
 // Division by T > 0 in round-to-nearest is monotone, so a search over ordinals finds it exactly:
