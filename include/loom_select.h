@@ -69,8 +69,9 @@ extern "C" {
 #define LOOM_SELECT_F32 0
 #define LOOM_SELECT_BF16 1
 
-/* Largest top_k the sampling kernels accept. */
+/* Largest top_k, and longest per-row history, the sampling kernels accept. */
 #define LOOM_SELECT_MAX_TOP_K 1024
+#define LOOM_SELECT_MAX_HISTORY 1024
 
 /* Returns a static English description of a status code. */
 LOOM_SELECT_API const char* loom_select_strerror(int status);
@@ -136,7 +137,8 @@ typedef struct loom_sample_params {
  *   (M = max y), accurate to 1e-5 relative on the probability scale.
  * With T == 0 the chain is greedy over the penalised row: the loom_argmax_rows rule picks the id,
  * out_prob = 1 and out_logp uses T = 1.
- * history may be NULL when history_len == 0. u is one uniform per row in [0, 1).
+ * history may be NULL when history_len == 0 (history_len <= LOOM_SELECT_MAX_HISTORY, else
+ * LOOM_SELECT_ESHAPE). u is one uniform per row in [0, 1).
  */
 LOOM_SELECT_API int loom_sample_rows(const void* logits, int dtype, int64_t rows, int64_t n_vocab, int64_t row_stride,
                      const int32_t* history, int32_t history_len, const float* u,

@@ -188,7 +188,7 @@ int loom_sample_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     a.out_topk = out_topk_ids;
     a.shard_out = nullptr;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * n_vocab, sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * n_vocab, kSampleCtasPerSm * sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 
@@ -223,7 +223,7 @@ int loom_sample_shard_partial(const void* logits, int dtype, int64_t rows, int64
     a.top_k = params->top_k;
     a.shard_out = out_records;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * shard_vocab, sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * shard_vocab, kSampleCtasPerSm * sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 

@@ -77,7 +77,8 @@ struct SampleLaunch {
     void* shard_out; // non-NULL: emit shard records instead of decisions
 };
 
-constexpr int kMaxHistory = 2048;
+constexpr int kMaxHistory = LOOM_SELECT_MAX_HISTORY;
+constexpr int kSampleCtasPerSm = 2;  // the sampler runs two CTAs per SM
 
 size_t sample_record_bytes(int32_t top_k);
 cudaError_t launch_sample_stream(const SampleLaunch& a, void* workspace, const WsLayout& l, int ctas,

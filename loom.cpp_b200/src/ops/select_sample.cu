@@ -32,19 +32,20 @@ namespace {
 
 constexpr int kSampWarps = 8;
 constexpr int kSampNT = kSampWarps * 32;
-constexpr int kSampStages = 4;
+constexpr int kSampCtasPerSm = kSampleCtasPerSm;  // two independent CTAs per SM overlap their latency-bound phases
+constexpr int kSampStages = 2;
 constexpr int kSampStageBytes = 32768;
-constexpr int kCandCap = 4096;    // candidate rank keys in shared memory
-constexpr int kSlots = 8;         // raw candidates a thread holds between prunes
-constexpr int kPruneSlack = 64;   // prune at a stage end when more than k + this many are held
-constexpr int kHashSlots = 4096;  // history hash set (load <= 1/2 at kMaxHistory ids)
+constexpr int kSlots = 4;           // raw candidates a thread holds between prunes
+constexpr int kCandCap = 2176;      // candidate rank keys in shared memory
+constexpr int kPruneSlack = 64;     // prune at a stage end when more than k + this many are held
+constexpr int kHashSlots = 2048;    // history hash set (load <= 1/2 at kMaxHistory ids)
 constexpr int kDecideSlots = 1024;
-static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kMaxHistory, "penalised entries of a stage must fit");
+constexpr uint32_t kPenalisedFlag = 0x80000000u;  // a raw slot holding a history id's raw value
 static_assert(kCandCap >= LOOM_SELECT_MAX_TOP_K + kPruneSlack + kSampNT * kSlots, "a prune's keys must fit");
 static_assert(LOOM_SELECT_MAX_TOP_K <= kDecideSlots && 2 * kDecideSlots <= kCandCap,
               "decision scratch e[] lives in key slots [1024, 2048)");
 static_assert(2 * kMaxHistory <= kHashSlots, "hash set load");
-static_assert(kSlots >= 8, "one vector's passes (8 bf16) must fit a thread's empty slots");
+static_assert(kHashSlots == 2048, "hash_slot takes 11 bits");
 
 struct SampleDev {
     float T, r, p;
@@ -123,7 +124,7 @@ __device__ __forceinline__ float smem_elem(const unsigned char* data, int32_t i)
 
 // History hash set: open addressing over global ids, -1 = empty.
 __device__ __forceinline__ uint32_t hash_slot(int32_t id) {
-    return (static_cast<uint32_t>(id) * 2654435761u) >> (32 - 12);  // 4096 slots
+    return (static_cast<uint32_t>(id) * 2654435761u) >> (32 - 11);  // 2048 slots
 }
 
 __device__ __forceinline__ bool hash_contains(const int32_t* set, int32_t id) {
@@ -150,26 +151,46 @@ __device__ __forceinline__ bool hash_insert(int32_t* set, int32_t id) {
 }
 
 // Tempers every thread's raw candidates into rank keys after the held ones, keeps the exact top-k,
-// sorted, in cand[0, K), raises the threshold to the k-th, and empties the slots. Every consumer
-// thread calls it with its own slot count `qn` (returned as 0).
+// sorted, in cand[0, K), raises the threshold to the k-th, and empties the slots. A raw slot with
+// kPenalisedFlag is a history id's raw value (penalised here); a raw slot without it that is a
+// history id is the stream's copy of that id and is dropped. Every consumer thread calls it with its
+// own slot count `qn` (returned as 0); hset is the segment's history set (unused without penalty).
 template <int kNT>
-__device__ void prune(const SampleDev p, uint64_t* cand, const uint2* slots, int& qn, SampleShared* sh) {
+__device__ void prune(const SampleDev p, uint64_t* cand, const uint2* slots, const int32_t* hset, int& qn,
+                      SampleShared* sh) {
     const int tid = threadIdx.x, lane = tid & 31;
-    int excl = qn;
+    uint64_t kk[kSlots];
+    int nk = 0;
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) {
+        kk[j] = 0ull;
+        if (j < qn) {
+            const uint2 e = slots[j * kNT + tid];
+            const int32_t id = static_cast<int32_t>(e.y & ~kPenalisedFlag);
+            float x = __uint_as_float(e.x);
+            bool keep = true;
+            if (e.y & kPenalisedFlag) x = penalise(x, p.r);
+            else if (p.penalty && hash_contains(hset, id)) keep = false;
+            if (keep) {
+                const float y = tempered(x, p.T, p.greedy);
+                if (y == y) kk[nk++] = loom_rank_key(y, id);  // (NaN never reaches a slot)
+            }
+        }
+    }
+    int excl = nk;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
         const int o = __shfl_up_sync(0xffffffffu, excl, off);
         if (lane >= off) excl += o;
     }
     const int wsum = __shfl_sync(0xffffffffu, excl, 31);
-    excl -= qn;
+    excl -= nk;
     int base = 0;
     if (lane == 0) base = atomicAdd(&sh->K, wsum);
     base = __shfl_sync(0xffffffffu, base, 0);
-    for (int j = 0; j < qn; ++j) {
-        const uint2 e = slots[j * kNT + tid];
-        cand[base + excl + j] = loom_rank_key(tempered(__uint_as_float(e.x), p.T, p.greedy), static_cast<int32_t>(e.y));
-    }
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j)
+        if (j < nk) cand[base + excl + j] = kk[j];
     qn = 0;
     group_sync<kNT>();
     const int n = sh->K;
@@ -371,25 +392,25 @@ struct SampleOp {
         const uint4* v4 = reinterpret_cast<const uint4*>(data);
         const int64_t gid0 = p.vocab_offset + col0;
 
-        // 1. the history ids this stage holds, with their penalised, tempered values
+        // 1. the history ids this stage holds: pending flagged raw entries, swept with the marks
+        //    (entry m of this thread's share of the list is bit m)
+        constexpr int kUniqPerThread = (kMaxHistory + kNT - 1) / kNT;
+        static_assert(kUniqPerThread <= 32, "pending history entries are one 32-bit word");
+        uint32_t pend = 0;
         if (p.penalty) {
             const int nu = sh->n_uniq;
-            const float thr = sh->thr_y;
-            for (int j = tid; j < nu; j += kNT) {
-                const int64_t c = static_cast<int64_t>(uniq[j]) - gid0;
-                if (c < 0 || c >= n) continue;
-                const float y = tempered(penalise(smem_elem<kDtype>(data, static_cast<int32_t>(c)), p.r), p.T, p.greedy);
-                if (p.lse) lse_offer(lse, y);
-                if (y == y && y >= thr) cand[atomicAdd(&sh->K, 1)] = loom_rank_key(y, static_cast<int32_t>(gid0 + c));
-            }
-            // Room: K <= k + kPruneSlack before the stage, plus nu here, plus every thread's full
-            // slots at the prune. Only very long histories with a large k can overflow: then the
-            // held keys are pruned right away.
-            if (p.k + kPruneSlack + nu + kSampNT * kSlots > kCandCap) {
-                group_sync<kNT>();
-                const bool need = sh->K > p.k + kPruneSlack;
-                group_sync<kNT>();  // every thread has read K before prune() changes it
-                if (need) prune<kNT>(p, cand, slots, qn, sh);
+#pragma unroll
+            for (int m = 0; m < kUniqPerThread; ++m) {
+                const int j = m * kNT + tid;
+                if (j < nu) {
+                    const int64_t c = static_cast<int64_t>(uniq[j]) - gid0;
+                    if (c >= 0 && c < n) {
+                        pend |= 1u << m;
+                        if (p.lse)
+                            lse_offer(lse, tempered(penalise(smem_elem<kDtype>(data, static_cast<int32_t>(c)), p.r),
+                                                    p.T, p.greedy));
+                    }
+                }
             }
         }
 
@@ -453,32 +474,44 @@ struct SampleOp {
             }
         }
 
-        // 4. sweep: each thread moves the passing elements of its marked vectors into its slots. A
-        //    thread whose slots cannot take a vector stops there (its marks stay) and, after the
-        //    prune, goes on (any one vector fits empty slots: kPer <= kSlots).
-        // Every round but the last sweeps at least one vector per stopped thread, so the bound is
+        // 4. sweep: each thread moves its pending history entries, then the passing elements of its
+        //    marked vectors, into its slots, element by element. A thread whose slots are full stops
+        //    there (its marks, pending bits and element cursor stay) and goes on after the prune.
+        // Every round but the last sweeps at least one element per stopped thread, so the bound is
         // never reached; it only guarantees that the loop ends.
+        const int max_rounds = (kVecsPerThread * kPer + kUniqPerThread) / kSlots + 3;
+        int qpos = 0;  // next element of the first marked vector
         for (int32_t round = 0;; ++round) {
             const float X = sh->X;  // rises at a prune
             bool stopped = false;
-            while (hits) {
-                const int i = __ffs(hits) - 1;
-                const int32_t v = i * kNT + tid;
-                Vec16<kDtype> e;
-                e.unpack(v4[v]);
-                const int64_t gv = gid0 + static_cast<int64_t>(v) * kPer;
-                uint32_t m = 0;
-#pragma unroll
-                for (int q = 0; q < kPer; ++q)
-                    if (e.x[q] >= X && !is_history(gv + q)) m |= 1u << q;
-                if (qn + __popc(m) > kSlots) {
+            while (pend) {
+                if (qn == kSlots) {
                     stopped = true;
                     break;
                 }
-#pragma unroll
-                for (int q = 0; q < kPer; ++q)
-                    if ((m >> q) & 1u)
-                        slots[(qn++) * kNT + tid] = make_uint2(__float_as_uint(e.x[q]), static_cast<uint32_t>(gv + q));
+                const int m = __ffs(pend) - 1;
+                const int32_t id = uniq[m * kNT + tid];
+                const float x = smem_elem<kDtype>(data, static_cast<int32_t>(id - gid0));
+                // with r >= 1 the penalty only lowers a value: one already below X cannot make the top-k
+                if (x == x && !(p.r >= 1.0f && x < X))
+                    slots[(qn++) * kNT + tid] = make_uint2(__float_as_uint(x), static_cast<uint32_t>(id) | kPenalisedFlag);
+                pend &= pend - 1u;
+            }
+            while (hits && !stopped) {
+                const int i = __ffs(hits) - 1;
+                const int32_t e0 = (i * kNT + tid) * kPer;  // element index of the vector in the stage
+                for (; qpos < kPer; ++qpos) {
+                    const float x = smem_elem<kDtype>(data, e0 + qpos);
+                    if (x >= X) {
+                        if (qn == kSlots) {
+                            stopped = true;
+                            break;
+                        }
+                        slots[(qn++) * kNT + tid] = make_uint2(__float_as_uint(x), static_cast<uint32_t>(gid0 + e0 + qpos));
+                    }
+                }
+                if (stopped) break;
+                qpos = 0;
                 hits &= hits - 1u;
             }
             if (stopped) sh->fail = 1;
@@ -490,9 +523,9 @@ struct SampleOp {
             for (int w = 0; w < kSampWarps; ++w) held += sh->wcnt[w];
             if (!failed && held <= p.k + kPruneSlack) break;
             group_sync<kNT>();
-            prune<kNT>(p, cand, slots, qn, sh);
+            prune<kNT>(p, cand, slots, hset, qn, sh);
             if (!failed) break;
-            if (round > kVecsPerThread + 1) {  // unreachable by construction (see above)
+            if (round > max_rounds) {  // unreachable by construction (see above)
                 if (tid == 0) record_status(p.status, LOOM_SELECT_ETIMEOUT);
                 break;
             }
@@ -514,7 +547,7 @@ struct SampleOp {
                 for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
             sh->seg_lse = a;
         }
-        prune<kNT>(p, cand, slots, qn, sh);  // also syncs
+        prune<kNT>(p, cand, slots, hset, qn, sh);  // also syncs
         const int K = sh->K;
         const LseAcc seg = sh->seg_lse;
         const bool bad = sh->bad != 0;
@@ -572,9 +605,10 @@ struct SampleOp {
 constexpr size_t kSampDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
                                 kSlots * kSampNT * sizeof(uint2) + kHashSlots * sizeof(int32_t) +
                                 kMaxHistory * sizeof(int32_t) + kDecideSlots * sizeof(double);
+static_assert(kSampDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
 
 template <int kDtype>
-__global__ void __launch_bounds__((kSampWarps + 1) * 32, 1) sample_stream_kernel(StreamGeom g, SampleDev p) {
+__global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_stream_kernel(StreamGeom g, SampleDev p) {
     extern __shared__ __align__(128) unsigned char dyn[];
     __shared__ StreamCtl ctl;
     __shared__ SampleShared sh;
@@ -642,7 +676,7 @@ __global__ void __launch_bounds__(kMergeNT) shard_merge_kernel(const unsigned ch
     const int K = topk_select_sorted<kMergeNT, kCandCap>(mcand, have, k, &tk);
     if (tid < 32) {
         double* e = reinterpret_cast<double*>(mcand + kDecideSlots);
-        double* S = e + kDecideSlots;
+        double* S = reinterpret_cast<double*>(mcand + kCandCap);
         decide_warp(mcand, K, top_p, __ldg(u + row), e, S, &sel_id, &sel_prob, &sel_y);
         if (tid == 0) {
             out_ids[row] = sel_id;
@@ -722,7 +756,7 @@ cudaError_t launch_sample_stream(const SampleLaunch& a, void* workspace, const W
 cudaError_t launch_shard_merge(const void* records, int32_t n_shards, int64_t rows, const float* u, int32_t top_k,
                                float top_p, int32_t* out_ids, float* out_prob, float* out_logp, int32_t* out_topk,
                                cudaStream_t stream) {
-    const size_t smem = kCandCap * sizeof(uint64_t);
+    const size_t smem = kCandCap * sizeof(uint64_t) + kDecideSlots * sizeof(double);
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

@@ -172,7 +172,7 @@ __device__ int topk_rank_sort(uint64_t* cand, int n, int k) {
 // first cut to k by the radix select, then ranked. n <= kCap (the buffer), k <= 1024.
 template <int kNT, int kCap>
 __device__ int topk_select_sorted(uint64_t* cand, int n, int k, TopkShared* sh) {
-    if (n > 2 * kNT) n = topk_select_compact<kNT, kCap / kNT>(cand, n, k, sh);
+    if (n > 2 * kNT) n = topk_select_compact<kNT, (kCap + kNT - 1) / kNT>(cand, n, k, sh);
     if (n <= kNT) return topk_rank_sort<kNT, 1>(cand, n, k);
     if (n <= 2 * kNT) return topk_rank_sort<kNT, 2>(cand, n, k);
     return topk_rank_sort<kNT, (1024 + kNT - 1) / kNT>(cand, n, k);
