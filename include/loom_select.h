@@ -146,6 +146,32 @@ LOOM_SELECT_API int loom_sample_rows(const void* logits, int dtype, int64_t rows
                      int32_t* out_topk_ids, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * loom_sample_rows for callers that cannot allocate device memory. No counterpart in loom.cpp (nor in
+ * this library's other entry points): it exists for hosts whose device memory is all handed out up
+ * front -- an engine whose own arena (ggml's backend allocator) sizes one buffer for the whole graph,
+ * a serving loop that may not grow its footprint after start-up, a plugin host with no allocation
+ * hook -- and so cannot give loom_sample_rows a workspace.
+ * Same arguments, checks and results as loom_sample_rows, without the workspace. Its scratch is one
+ * fixed device array inside the library (LOOM_SELECT_NOALLOC_SCRATCH_BYTES per device), so:
+ *   - top_k is limited to LOOM_SELECT_NOALLOC_MAX_TOP_K; a larger one returns LOOM_SELECT_ESHAPE;
+ *   - each call clears the array's status word and tickets itself (a memset on `stream`);
+ *   - calls whose work can overlap on the GPU (other streams, other host threads) race on the array:
+ *     order them on one stream;
+ *   - the first call on a device looks the array up and loads its code there; make it before any
+ *     stream capture;
+ *   - out_status (device int32, may be NULL) receives the call's device-side status
+ *     (LOOM_SELECT_EHISTORY, LOOM_SELECT_ETIMEOUT or 0), the word loom_select_read_status reads for
+ *     a caller-owned workspace.
+ */
+#define LOOM_SELECT_NOALLOC_MAX_TOP_K 64
+#define LOOM_SELECT_NOALLOC_SCRATCH_BYTES 1089792 /* 256 + 8192 + 2048 * (16 + 8 * 64) */
+
+LOOM_SELECT_API int loom_sample_rows_noalloc(const void* logits, int dtype, int64_t rows, int64_t n_vocab,
+                             int64_t row_stride, const int32_t* history, int32_t history_len, const float* u,
+                             const loom_sample_params* params, int32_t* out_ids, float* out_prob,
+                             float* out_logp, int32_t* out_topk_ids, int32_t* out_status, void* stream);
+
+/*
  * Vocabulary-sharded sampling: each GPU owns ids [vocab_offset, vocab_offset + shard_vocab) of a
  * vocabulary of vocab_total ids and runs loom_sample_shard_partial on its [rows, shard_vocab] slice.
  * The per-row records (loom_shard_record_bytes(top_k) bytes each, `rows` records) are then gathered

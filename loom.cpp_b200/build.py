@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libloom_select.so")
 OBJDIR = os.path.join(ROOT, "_build", "loom_select")
 
-SOURCES = ["select_capi.cu", "select_argmax.cu", "select_ctc.cu", "select_sample.cu"]
+SOURCES = ["select_capi.cu", "select_argmax.cu", "select_ctc.cu", "select_sample.cu", "select_noalloc.cu"]
 
 # sm_100a only. --fmad=false: no multiply-add contraction anywhere, so every float expression
 # rounds as written (the decision arithmetic also spells its operations as explicit intrinsics).

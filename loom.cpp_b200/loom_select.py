@@ -49,6 +49,7 @@ EXPORTS = (
     "loom_select_read_status",
     "loom_argmax_rows",
     "loom_sample_rows",
+    "loom_sample_rows_noalloc",
     "loom_shard_record_bytes",
     "loom_sample_shard_partial",
     "loom_sample_shard_merge",
@@ -93,6 +94,8 @@ def _lib():
             "loom_argmax_rows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
             "loom_sample_rows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, i32, vp,
                                                 ctypes.POINTER(SampleParams), vp, vp, vp, vp, vp, sz, vp]),
+            "loom_sample_rows_noalloc": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, i32, vp,
+                                                        ctypes.POINTER(SampleParams), vp, vp, vp, vp, vp, vp]),
             "loom_shard_record_bytes": (sz, [i32]),
             "loom_sample_shard_partial": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, i64, i64, vp, i32,
                                                          ctypes.POINTER(SampleParams), vp, vp, sz, vp]),
@@ -245,6 +248,20 @@ def sample_rows_into(logits, u, out_ids, out_prob, temperature, repetition_penal
                                   _ptr(u), ctypes.byref(p), _ptr(out_ids), _ptr(out_prob), _ptr(out_logp),
                                   _ptr(out_topk), _ptr(buf), buf.numel(), _stream_handle(stream)),
           "loom_sample_rows")
+
+
+def sample_rows_noalloc_into(logits, u, out_ids, out_prob, temperature, repetition_penalty=1.0, top_k=40,
+                             top_p=1.0, history=None, out_logp=None, out_topk=None, out_status=None, stream=None):
+    """sample_rows_into without a workspace: the library's own fixed scratch (top_k <= 64; calls must
+    not overlap on the GPU). out_status: an int32 device tensor of one element, or None."""
+    rows, n_vocab, stride = _rows_view(logits)
+    hl = 0 if history is None else int(history.shape[-1])
+    p = SampleParams(temperature, repetition_penalty, top_k, top_p)
+    check(_lib().loom_sample_rows_noalloc(_ptr(logits), _dtype_code(logits), rows, n_vocab, stride, _ptr(history),
+                                          hl, _ptr(u), ctypes.byref(p), _ptr(out_ids), _ptr(out_prob),
+                                          _ptr(out_logp), _ptr(out_topk), _ptr(out_status),
+                                          _stream_handle(stream)),
+          "loom_sample_rows_noalloc")
 
 
 def sample_rows(logits, u, temperature, repetition_penalty=1.0, top_k=40, top_p=1.0, history=None,
