@@ -59,13 +59,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for at most kSuspendHintNs: a
+// waiting warp sleeps instead of spinning, so it takes no issue slots from the warps that work.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return done != 0;
+}
+
 // Waits for the phase of `bar` with the given parity to complete; false (and a recorded timeout)
 // if it does not within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
         if (global_timer_ns() - t0 > kWaitLimitNs) {
             record_status(status_word, LOOM_SELECT_ETIMEOUT);
             return false;

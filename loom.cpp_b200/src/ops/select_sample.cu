@@ -91,6 +91,9 @@ struct SampleShared {
     int32_t sel_id;
     float sel_prob;
     float sel_y;
+    unsigned long long key_t;  // warp path: every kept key reaches this (a k-th best key, or a value floor)
+    uint32_t x_key;            // warp path: order key of the raw threshold X
+    float wq[kSampWarps];      // warp path: per warp, a raw value that ceil(k / warps) of its lanes' maxima reach
 };
 
 __device__ __forceinline__ float neg_inf() { return -__int_as_float(0x7f800000); }
@@ -212,8 +215,8 @@ __device__ void prune(const SampleDev p, uint64_t* cand, const uint2* slots, con
 // The K (<= k) best keys of a whole row, sorted: fill up to k with NaN ids when the row has fewer
 // than k non-NaN values, then emit the row's result (a decision, or a shard record).
 template <int kDtype, int kNT>
-__device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row, uint64_t* cand, double* S, int K,
-                             LseAcc lse, bool bad, SampleShared* sh) {
+__device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row, uint64_t* cand, double* e, double* S,
+                             int K, LseAcc lse, bool bad, SampleShared* sh) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     const unsigned char* rowp = g.base + row * g.row_stride * kEsz;
@@ -288,7 +291,6 @@ __device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row,
         return;
     }
     if (warp == 0) {
-        double* e = reinterpret_cast<double*>(cand + kDecideSlots);
         if (p.greedy) {
             if (lane == 0) {
                 const float x0 = load_global_elem<kDtype>(rowp, 0);
@@ -319,8 +321,65 @@ __device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row,
     group_sync<kNT>();
 }
 
+// The end of a row segment, once its K best keys are sorted in cand[0, K): a whole row is finalised
+// here; a piece of a split row writes its record and takes the row's ticket, and the CTA that takes
+// the last ticket merges every piece's record and finalises the row. cand holds kCap keys.
+template <int kDtype, int kNT, int kCap>
+__device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segment& s, uint64_t* cand, double* e,
+                               double* S, int K, LseAcc seg, bool bad, SampleShared* sh) {
+    const int tid = threadIdx.x;
+    if (s.count == 1) {
+        finalize_row<kDtype, kNT>(p, g, s.row, cand, e, S, K, seg, bad, sh);
+        return;
+    }
+    // a piece of a split row: write its record, take a ticket, the last one merges
+    unsigned char* rec = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + s.index, s.row)) * p.rec_bytes;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(rec + 16);
+    for (int j = tid; j < K; j += kNT) keys[j] = cand[j];
+    if (tid == 0) {
+        RecordHead* h = reinterpret_cast<RecordHead*>(rec);
+        h->count = bad ? -1 : K;
+        h->m = seg.m;
+        h->s = seg.s;
+        h->reserved = 0;
+    }
+    __threadfence();
+    group_sync<kNT>();
+    if (tid == 0) {
+        const int prev = atomicAdd(&p.tickets[record_slot(g, s.first_cta, s.row)], 1);
+        sh->last = prev == s.count - 1;
+    }
+    group_sync<kNT>();
+    if (!sh->last) return;
+    __threadfence();
+    // merge every piece's record
+    int have = 0;
+    bool any_bad = false;
+    LseAcc tot = lse_init();
+    for (int j = 0; j < s.count; ++j) {
+        const unsigned char* r = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j, s.row)) * p.rec_bytes;
+        const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
+        if (c < 0) {
+            any_bad = true;
+            continue;
+        }
+        LseAcc part;
+        part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
+        part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
+        tot = lse_merge(tot, part);
+        if (have + c > kCap) have = topk_select_sorted<kNT, kCap>(cand, have, p.k, &sh->tk);
+        const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
+        for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
+        have += c;
+        group_sync<kNT>();
+    }
+    const int Kf = topk_select_sorted<kNT, kCap>(cand, have, p.k, &sh->tk);
+    if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
+    finalize_row<kDtype, kNT>(p, g, s.row, cand, e, S, Kf, tot, any_bad, sh);
+}
+
 template <int kDtype>
-struct SampleOp {
+struct WideSampleOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     static constexpr int kPer = 16 / kEsz;
     static constexpr int kNT = kSampNT;
@@ -548,67 +607,19 @@ struct SampleOp {
             sh->seg_lse = a;
         }
         prune<kNT>(p, cand, slots, hset, qn, sh);  // also syncs
-        const int K = sh->K;
-        const LseAcc seg = sh->seg_lse;
-        const bool bad = sh->bad != 0;
-        if (s.count == 1) {
-            finalize_row<kDtype, kNT>(p, g, s.row, cand, S, K, seg, bad, sh);
-            return;
-        }
-        // a piece of a split row: write its record, take a ticket, the last one merges
-        unsigned char* rec = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + s.index, s.row)) * p.rec_bytes;
-        uint64_t* keys = reinterpret_cast<uint64_t*>(rec + 16);
-        for (int j = tid; j < K; j += kNT) keys[j] = cand[j];
-        if (tid == 0) {
-            RecordHead* h = reinterpret_cast<RecordHead*>(rec);
-            h->count = bad ? -1 : K;
-            h->m = seg.m;
-            h->s = seg.s;
-            h->reserved = 0;
-        }
-        __threadfence();
-        group_sync<kNT>();
-        if (tid == 0) {
-            const int prev = atomicAdd(&p.tickets[record_slot(g, s.first_cta, s.row)], 1);
-            sh->last = prev == s.count - 1;
-        }
-        group_sync<kNT>();
-        if (!sh->last) return;
-        __threadfence();
-        // merge every piece's record
-        int have = 0;
-        bool any_bad = false;
-        LseAcc tot = lse_init();
-        for (int j = 0; j < s.count; ++j) {
-            const unsigned char* r = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j, s.row)) * p.rec_bytes;
-            const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
-            if (c < 0) {
-                any_bad = true;
-                continue;
-            }
-            LseAcc part;
-            part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
-            part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
-            tot = lse_merge(tot, part);
-            if (have + c > kCandCap) have = topk_select_sorted<kNT, kCandCap>(cand, have, p.k, &sh->tk);
-            const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
-            for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
-            have += c;
-            group_sync<kNT>();
-        }
-        const int Kf = topk_select_sorted<kNT, kCandCap>(cand, have, p.k, &sh->tk);
-        if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
-        finalize_row<kDtype, kNT>(p, g, s.row, cand, S, Kf, tot, any_bad, sh);
+        finish_segment<kDtype, kNT, kCandCap>(p, g, s, cand, reinterpret_cast<double*>(cand + kDecideSlots), S, sh->K,
+                                             sh->seg_lse, sh->bad != 0, sh);
     }
 };
 
-constexpr size_t kSampDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
+constexpr size_t kWideDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes + kCandCap * sizeof(uint64_t) +
                                 kSlots * kSampNT * sizeof(uint2) + kHashSlots * sizeof(int32_t) +
                                 kMaxHistory * sizeof(int32_t) + kDecideSlots * sizeof(double);
-static_assert(kSampDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
+static_assert(kWideDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
 
+// Lockstep kernel for top_k above the warp path's limit.
 template <int kDtype>
-__global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_stream_kernel(StreamGeom g, SampleDev p) {
+__global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_wide_kernel(StreamGeom g, SampleDev p) {
     extern __shared__ __align__(128) unsigned char dyn[];
     __shared__ StreamCtl ctl;
     __shared__ SampleShared sh;
@@ -618,8 +629,496 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
     int32_t* hset = reinterpret_cast<int32_t*>(slots + kSlots * kSampNT);
     int32_t* uniq = hset + kHashSlots;
     double* S = reinterpret_cast<double*>(uniq + kMaxHistory);
-    SampleOp<kDtype> op{g, p, &sh, cand, slots, hset, uniq, S, lse_init(), 0, true};
+    WideSampleOp<kDtype> op{g, p, &sh, cand, slots, hset, uniq, S, lse_init(), 0, true};
     stream_ranges<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
+}
+
+// ---------------------------------------------------------------------------------------------
+// The warp path (top_k <= kWarpMaxK). Consumer warps run free of one another between segment
+// boundaries (stream_ranges_warps): no CTA barrier per stage. Each warp appends the raw (value, id)
+// pairs that reach the raw threshold X to a buffer of its own, one ballot per step. When the buffer
+// is full the warp alone tempers it into rank keys, keeps its best k (a register bitonic sort) and
+// raises the CTA's thresholds with shared-memory atomics: key_t, which every kept key reaches, and X,
+// the raw bound derived from it. Both only rise, so a warp that reads them late keeps more than it
+// needs, never less. What raises them in the common case costs one max per vector: every lane keeps
+// the running maximum of the non-history elements it has read in the segment; after a stage a warp
+// publishes the ceil(k / warps)-th largest of its 32 lanes' maxima, and the smallest published value
+// is reached by at least k distinct elements (the lanes' element sets are disjoint), so it bounds the
+// k-th best from below. The stream skips history ids' raw values (a hash lookup, only for elements
+// that pass X); at the segment end the CTA reads their logits again from global memory (the row has
+// just gone through L2), penalises and tempers them, and offers them against the final threshold.
+// A segment ends with every warp's best k merged by the whole CTA (exact selection, then the
+// decision).
+
+constexpr int kWarpMaxK = 128;                    // the warp path serves top_k up to this
+constexpr int kRawCap = 128;                      // raw pairs a warp holds between its prunes
+constexpr int kWarpKeyCap = kWarpMaxK + kRawCap;  // a warp's kept keys plus one tempered raw batch
+constexpr int kWarpCand = kSampWarps * kRawCap;   // the segment-end gather (aliases the raw buffers)
+static_assert(kSampWarps * kWarpMaxK <= kWarpCand, "the warps' best k keys fit the gather");
+static_assert(kWarpKeyCap <= 256, "a warp sorts at most 8 keys per lane");
+static_assert(2 * kWarpMaxK * sizeof(double) <= kSampWarps * kWarpKeyCap * sizeof(uint64_t),
+              "decision scratch fits the key buffers");
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// Descending bitonic sort of 32 * P keys held P per lane (element j * 32 + lane in a[j]).
+template <int P>
+__device__ __forceinline__ void warp_sort_keys_desc(uint64_t (&a)[P]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32 * P; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= 32) {
+                const int js = stride >> 5;
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    if ((j & js) == 0) {
+                        const int j2 = j | js;
+                        const bool desc = ((j * 32) & size) == 0;
+                        const uint64_t lo = a[j], hi = a[j2];
+                        const bool swap = desc ? (lo < hi) : (lo > hi);
+                        a[j] = swap ? hi : lo;
+                        a[j2] = swap ? lo : hi;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, a[j], stride);
+                    const bool lower = (lane & stride) == 0;
+                    const bool desc = ((j * 32 + lane) & size) == 0;
+                    const uint64_t big = a[j] > o ? a[j] : o, small = a[j] > o ? o : a[j];
+                    a[j] = (lower == desc) ? big : small;
+                }
+            }
+        }
+    }
+}
+
+template <int P>
+__device__ int warp_keep_best_p(uint64_t* w, int n, int k) {
+    const int lane = threadIdx.x & 31;
+    uint64_t a[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+        const int i = j * 32 + lane;
+        a[j] = i < n ? w[i] : 0ull;  // 0 ranks below every real key
+    }
+    __syncwarp();
+    warp_sort_keys_desc<P>(a);
+    const int K = n < k ? n : k;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+        const int i = j * 32 + lane;
+        if (i < K) w[i] = a[j];
+    }
+    __syncwarp();
+    return K;
+}
+
+// Sorts a warp's keys w[0, n) (n <= 256) best-first and keeps the best min(n, k) in w[0, ...).
+__device__ int warp_keep_best(uint64_t* w, int n, int k) {
+    if (n <= 32) return warp_keep_best_p<1>(w, n, k);
+    if (n <= 64) return warp_keep_best_p<2>(w, n, k);
+    if (n <= 128) return warp_keep_best_p<4>(w, n, k);
+    return warp_keep_best_p<8>(w, n, k);
+}
+
+// Maximum of one 16-byte vector of logits (NaN elements ignored; NaN only if all are NaN).
+template <int kDtype>
+__device__ __forceinline__ float vec_max(uint4 raw) {
+    Vec16<kDtype> e;
+    e.unpack(raw);
+    if constexpr (kDtype == LOOM_SELECT_BF16) {
+        return fmaxf(fmaxf(fmaxf(e.x[0], e.x[1]), fmaxf(e.x[2], e.x[3])),
+                     fmaxf(fmaxf(e.x[4], e.x[5]), fmaxf(e.x[6], e.x[7])));
+    } else {
+        return fmaxf(fmaxf(e.x[0], e.x[1]), fmaxf(e.x[2], e.x[3]));
+    }
+}
+
+template <int kDtype>
+struct WarpSampleOp {
+    static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
+    static constexpr int kPer = 16 / kEsz;
+    static constexpr int kNT = kSampNT;
+    StreamGeom g;  // copies: no pointer into the kernel's parameters
+    SampleDev p;
+    SampleShared* sh;
+    uint2* raw;         // this warp's raw pairs (value bits, global id) [kRawCap]
+    uint64_t* wk;       // this warp's kept keys [kWarpKeyCap]
+    uint64_t* cand;     // segment-end gather [kWarpCand] (the raw buffers of all warps)
+    uint64_t* keys0;    // all warps' key buffers (decision scratch at a segment end)
+    int32_t* hset;      // history hash set of the segment
+    int32_t* uniq;      // its distinct ids, as a list
+    LseAcc lse;
+    int nr;      // raw pairs this warp holds (the same in every lane)
+    int nk;      // keys this warp keeps
+    int stage;   // stage index within the segment
+    float rmax;    // this lane's running maximum over the non-history elements it has read
+    float wv;      // this warp's published value (sh->wq[warp])
+    bool crossed;  // rmax has risen above wv since the last publish
+
+    __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
+    __device__ const int32_t* row_hist(int64_t row) const { return p.hist + row * static_cast<int64_t>(p.hist_len); }
+
+    __device__ __forceinline__ bool is_history(int64_t gid) const {
+        return p.penalty && hash_contains(hset, static_cast<int32_t>(gid));
+    }
+
+    __device__ __forceinline__ float threshold_X() const {
+        return order_key_to_float(*reinterpret_cast<const volatile uint32_t*>(&sh->x_key));
+    }
+
+    // One lane: k kept keys reach `kth`, so the row's k-th best does too.
+    __device__ void raise(uint64_t kth) {
+        const unsigned long long old = atomicMax(&sh->key_t, static_cast<unsigned long long>(kth));
+        if (kth > old) atomicMax(&sh->x_key, loom_order_key(inverse_threshold_bound(rank_key_value(kth), p.T, p.greedy)));
+    }
+
+    // One lane: at least k distinct non-history elements have a raw value >= v.
+    __device__ void raise_raw(float v) {
+        const float t = tempered(v, p.T, p.greedy);
+        if (!(t > neg_inf())) return;  // (-inf or NaN: nothing to raise)
+        const unsigned long long floor = static_cast<unsigned long long>(loom_order_key(t)) << 32;
+        const unsigned long long old = atomicMax(&sh->key_t, floor);
+        if (floor > old) atomicMax(&sh->x_key, loom_order_key(inverse_threshold_bound(t, p.T, p.greedy)));
+    }
+
+    // Warp-collective: when a lane's maximum has crossed the published value since the last call
+    // (`crossed`), publishes this warp's
+    // ceil(k / warps)-th largest lane maximum and raises the thresholds to the smallest value the
+    // warps have published. (Only a crossing can change that order statistic.)
+    __device__ void publish() {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        if (!__any_sync(0xffffffffu, crossed)) return;
+        crossed = false;
+        const float sorted = warp_sort_desc(rmax);
+        const float v = __shfl_sync(0xffffffffu, sorted, (p.k + kSampWarps - 1) / kSampWarps - 1);
+        if (!(v > wv)) return;
+        wv = v;
+        if (lane == 0) {
+            volatile float* wq = sh->wq;
+            wq[warp] = v;
+            float mn = v;
+            for (int w = 0; w < kSampWarps; ++w) mn = fminf(mn, wq[w]);
+            raise_raw(mn);
+        }
+    }
+
+    // Warp-collective: tempers the raw pairs into keys after the kept ones (dropping those under
+    // key_t), keeps the best k and, holding k, raises the thresholds to the k-th.
+    __device__ void prune() {
+        if (nr == 0) return;
+        const int lane = threadIdx.x & 31;
+        __syncwarp();
+        const uint64_t floor = *reinterpret_cast<const volatile unsigned long long*>(&sh->key_t);
+        int n = nk;
+        for (int base = 0; base < nr; base += 32) {
+            const int i = base + lane;
+            uint64_t key = 0ull;
+            bool keep = false;
+            if (i < nr) {
+                const uint2 e = raw[i];
+                key = loom_rank_key(tempered(__uint_as_float(e.x), p.T, p.greedy), static_cast<int32_t>(e.y));
+                keep = key >= floor;
+            }
+            const uint32_t b = __ballot_sync(0xffffffffu, keep);
+            if (keep) wk[n + __popc(b & lanemask_lt())] = key;
+            n += __popc(b);
+        }
+        nr = 0;
+        __syncwarp();
+        if (n >= p.k) {
+            n = warp_keep_best(wk, n, p.k);
+            if (lane == 0) raise(wk[p.k - 1]);
+        }
+        nk = n;
+    }
+
+    // Warp-collective: the lanes with `take` append (x, id); a full buffer is pruned first.
+    __device__ __forceinline__ void append(bool take, float x, int32_t id) {
+        const uint32_t b = __ballot_sync(0xffffffffu, take);
+        if (b == 0u) return;
+        const int c = __popc(b);
+        if (nr + c > kRawCap) prune();
+        if (take) raw[nr + __popc(b & lanemask_lt())] = make_uint2(__float_as_uint(x), static_cast<uint32_t>(id));
+        nr += c;
+    }
+
+    __device__ void begin_segment(const Segment& s) {
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        if (tid == 0) {
+            sh->K = 0;
+            sh->bad = 0;
+            sh->n_uniq = 0;
+            sh->warm_key = 0xffffffffu;
+            sh->key_t = 0ull;
+            sh->x_key = loom_order_key(neg_inf());
+            for (int w = 0; w < kSampWarps; ++w) sh->wq[w] = neg_inf();
+        }
+        lse = lse_init();
+        nr = 0;
+        nk = 0;
+        stage = 0;
+        rmax = neg_inf();
+        wv = neg_inf();
+        crossed = false;
+        if (p.penalty) {
+            int4* h4 = reinterpret_cast<int4*>(hset);
+            for (int i = tid; i < kHashSlots / 4; i += kNT) h4[i] = make_int4(-1, -1, -1, -1);
+        }
+        group_sync<kNT>();
+        // validate the whole history; the distinct ids inside this segment go into the set and list
+        const int64_t seg_lo = p.vocab_offset + s.j0, seg_hi = p.vocab_offset + s.j1;
+        for (int j = tid; j < p.hist_len; j += kNT) {
+            const int32_t id = __ldg(row_hist(s.row) + j);
+            if (id < 0 || id >= p.vocab_limit) sh->bad = 1;
+            else if (p.penalty && id >= seg_lo && id < seg_hi && hash_insert(hset, id))
+                uniq[atomicAdd(&sh->n_uniq, 1)] = id;
+        }
+        group_sync<kNT>();
+        if (tid == 0 && sh->bad) record_status(p.status, LOOM_SELECT_EHISTORY);
+        // edges (at most 14 elements outside the 16-byte-aligned interior), read by warp 0
+        if (warp == 0) {
+            const int32_t n_edges = segment_edge_count(s, kEsz);
+            bool take = false;
+            float x = 0.0f;
+            int32_t gid = 0;
+            if (lane < n_edges) {
+                const int64_t col = segment_edge_col(s, kEsz, lane);
+                x = load_global_elem<kDtype>(row_ptr(s.row), col);
+                gid = static_cast<int32_t>(p.vocab_offset + col);
+                if (is_history(gid)) x = penalise(x, p.r);
+                if (p.lse) lse_offer(lse, tempered(x, p.T, p.greedy));
+                take = x == x;
+            }
+            append(take, x, gid);
+        }
+    }
+
+    // The first stage of a segment seeds the thresholds (every warp, two CTA barriers): each warp
+    // sorts its lanes' maxima (a lane whose maximum is a history id vouches for nothing) and the
+    // smallest of the warps' ceil(k / warps)-th largest is a value that at least k elements reach.
+    __device__ void warm_up(const uint4* v4, int32_t nvec, int64_t gid0, bool live) {
+        const int tid = threadIdx.x, lane = tid & 31;
+        float m = neg_inf();
+        if (live) {
+            int64_t at = -1;
+            for (int32_t v = tid; v < nvec; v += kNT) {
+                Vec16<kDtype> e;
+                e.unpack(v4[v]);
+#pragma unroll
+                for (int q = 0; q < kPer; ++q)
+                    if (e.x[q] > m) {
+                        m = e.x[q];
+                        at = gid0 + static_cast<int64_t>(v) * kPer + q;
+                    }
+            }
+            if (at >= 0 && is_history(at)) m = neg_inf();
+        }
+        rmax = m;
+        const float sorted = warp_sort_desc(m);
+        const int q = (p.k + kSampWarps - 1) / kSampWarps;  // <= 16
+        const float bw = __shfl_sync(0xffffffffu, sorted, q - 1);
+        wv = bw;
+        if (lane == 0) {
+            sh->wq[threadIdx.x >> 5] = bw;
+            atomicMin(&sh->warm_key, loom_order_key(bw));
+        }
+        group_sync<kNT>();
+        if (tid == 0) {
+            const float ty = tempered(order_key_to_float(sh->warm_key), p.T, p.greedy);
+            if (ty == ty && ty > neg_inf()) {
+                atomicMax(&sh->key_t, static_cast<unsigned long long>(loom_order_key(ty)) << 32);
+                atomicMax(&sh->x_key, loom_order_key(inverse_threshold_bound(ty, p.T, p.greedy)));
+            }
+        }
+        group_sync<kNT>();
+    }
+
+    __device__ void chunk(const Segment&, const unsigned char* data, int64_t col0, int32_t n, bool live) {
+        const int tid = threadIdx.x;
+        const int32_t nvec = n / kPer;
+        const uint4* v4 = reinterpret_cast<const uint4*>(data);
+        const int64_t gid0 = p.vocab_offset + col0;
+        const int st = stage++;
+        if (st == 0) warm_up(v4, nvec, gid0, live);
+        if (!live) return;
+        const float X = threshold_X();
+
+        // 2. mark. The common path is one max per element: each vector's maximum mu[i] (NaN for a
+        //    vector past the stage's end) and the lane's stage maximum smax; only a lane whose smax
+        //    reaches X (rare) turns its mu[i] into marks.
+        constexpr int kVecsPerThread = kSampStageBytes / 16 / kNT;
+        static_assert(kVecsPerThread <= 32, "marks are one 32-bit word");
+        float mu[kVecsPerThread];
+        float smax = neg_inf();
+        if (nvec == kVecsPerThread * kNT && !p.lse) {
+#pragma unroll
+            for (int i = 0; i < kVecsPerThread; ++i) {
+                mu[i] = vec_max<kDtype>(v4[i * kNT + tid]);
+                smax = fmaxf(smax, mu[i]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kVecsPerThread; ++i) {
+                const int32_t v = i * kNT + tid;
+                mu[i] = __int_as_float(0x7fc00000);
+                if (v < nvec) {
+                    Vec16<kDtype> e;
+                    e.unpack(v4[v]);
+                    mu[i] = vec_max<kDtype>(v4[v]);
+                    if (p.lse) {
+                        // every element once (history ids are offered at the segment end)
+#pragma unroll
+                        for (int q = 0; q < kPer; ++q)
+                            if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q))
+                                lse_offer(lse, tempered(e.x[q], p.T, p.greedy));
+                    }
+                }
+                smax = fmaxf(smax, mu[i]);
+            }
+        }
+        uint32_t hits = 0;
+        if (smax >= X) {
+#pragma unroll
+            for (int i = 0; i < kVecsPerThread; ++i) hits |= static_cast<uint32_t>(mu[i] >= X) << i;
+        }
+
+        // The running maximum. Values at or below the published wv never decide the published order
+        // statistic (it only rises), so only a rise above wv must be a non-history element's value:
+        // that rare case finds the vector holding the maximum (from mu[]) and skips the rise when the
+        // maximum there is a history id's raw value.
+        if (smax > rmax) {
+            bool ok = true;
+            if (p.penalty && smax > wv) {
+                int at = 0;
+#pragma unroll
+                for (int i = kVecsPerThread - 1; i >= 0; --i)
+                    if (mu[i] == smax) at = i;
+                const int32_t v = at * kNT + tid;
+                Vec16<kDtype> e;
+                e.unpack(v4[v]);
+                ok = false;
+#pragma unroll
+                for (int q = 0; q < kPer; ++q)
+                    if (e.x[q] == smax && !is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) ok = true;
+            }
+            if (ok) {
+                crossed = crossed || (rmax <= wv && smax > wv);
+                rmax = smax;
+            }
+        }
+        if (st < 4 || (st & 3) == 3) publish();  // every stage at first, then every fourth at most
+
+        // 3. sweep: one passing element per lane per step, appended by ballot
+        if (__any_sync(0xffffffffu, hits != 0u)) {
+            uint32_t m = 0u;  // pass bits of the vector this lane is sweeping
+            int32_t e0 = 0;   // its first element in the stage
+            for (;;) {
+                while (m == 0u && hits != 0u) {
+                    const int i = __ffs(hits) - 1;
+                    hits &= hits - 1u;
+                    const int32_t v = i * kNT + tid;
+                    Vec16<kDtype> e;
+                    e.unpack(v4[v]);
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q) m |= static_cast<uint32_t>(e.x[q] >= X) << q;
+                    e0 = v * kPer;
+                }
+                const bool has = m != 0u;
+                if (!__any_sync(0xffffffffu, has)) break;
+                bool take = false;
+                float x = 0.0f;
+                int32_t id = 0;
+                if (has) {
+                    const int q = __ffs(m) - 1;
+                    m &= m - 1u;
+                    x = smem_elem<kDtype>(data, e0 + q);
+                    id = static_cast<int32_t>(gid0 + e0 + q);
+                    take = !is_history(id);  // a history id's stream value is replaced at the segment end
+                }
+                append(take, x, id);
+            }
+        }
+    }
+
+    __device__ void end_segment(const Segment& s) {
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        prune();  // at most k keys per warp, the raw buffer empty
+        if (p.penalty) {
+            // The segment's distinct history ids with their penalised, tempered values, read from
+            // global memory (the row has just streamed through L2), against the final threshold.
+            const int nu = sh->n_uniq;
+            const uint64_t floor = *reinterpret_cast<const volatile unsigned long long*>(&sh->key_t);
+            for (int base = warp * 32; base < nu; base += kNT) {  // warp-uniform trip count
+                const int j = base + lane;
+                uint64_t key = 0ull;
+                bool keep = false;
+                if (j < nu) {
+                    const int32_t id = uniq[j];
+                    const float x = load_global_elem<kDtype>(row_ptr(s.row), static_cast<int64_t>(id) - p.vocab_offset);
+                    const float y = tempered(penalise(x, p.r), p.T, p.greedy);
+                    if (p.lse) lse_offer(lse, y);
+                    key = loom_rank_key(y, id);
+                    keep = y == y && key >= floor;
+                }
+                const uint32_t b = __ballot_sync(0xffffffffu, keep);
+                if (keep) wk[nk + __popc(b & lanemask_lt())] = key;
+                nk += __popc(b);
+            }
+            __syncwarp();
+            if (nk > p.k) nk = warp_keep_best(wk, nk, p.k);
+        }
+        if (p.lse) {
+            const LseAcc w = lse_warp_reduce(lse);
+            if (lane == 0) sh->lse_w[warp] = w;
+        }
+        group_sync<kNT>();  // every raw buffer is empty: the gather (which aliases them) is free
+        int off = 0;
+        if (lane == 0) off = atomicAdd(&sh->K, nk);
+        off = __shfl_sync(0xffffffffu, off, 0);
+        for (int i = lane; i < nk; i += 32) cand[off + i] = wk[i];
+        if (tid == 0) {
+            LseAcc a = lse_init();
+            if (p.lse)
+                for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
+            sh->seg_lse = a;
+        }
+        group_sync<kNT>();
+        const int K = topk_select_sorted<kNT, kWarpCand>(cand, sh->K, p.k, &sh->tk);
+        double* e = reinterpret_cast<double*>(keys0);
+        finish_segment<kDtype, kNT, kWarpCand>(p, g, s, cand, e, e + kWarpMaxK, K, sh->seg_lse, sh->bad != 0, sh);
+    }
+};
+
+constexpr size_t kWarpDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes +
+                                kSampWarps * kRawCap * sizeof(uint2) + kSampWarps * kWarpKeyCap * sizeof(uint64_t) +
+                                kHashSlots * sizeof(int32_t) + kMaxHistory * sizeof(int32_t);
+static_assert(kWarpDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
+
+template <int kDtype>
+__global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_stream_kernel(StreamGeom g, SampleDev p) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    __shared__ StreamCtl ctl;
+    __shared__ SampleShared sh;
+    unsigned char* ring = dyn;
+    uint2* raw_all = reinterpret_cast<uint2*>(dyn + static_cast<size_t>(kSampStages) * kSampStageBytes);
+    uint64_t* keys_all = reinterpret_cast<uint64_t*>(raw_all + kSampWarps * kRawCap);
+    int32_t* hset = reinterpret_cast<int32_t*>(keys_all + kSampWarps * kWarpKeyCap);
+    int32_t* uniq = hset + kHashSlots;
+    const int warp = threadIdx.x >> 5;
+    const int w = warp < kSampWarps ? warp : 0;  // the producer warp holds no buffers
+    WarpSampleOp<kDtype> op{g,     p,    &sh,  raw_all + w * kRawCap, keys_all + w * kWarpKeyCap,
+                            reinterpret_cast<uint64_t*>(raw_all), keys_all, hset, uniq, lse_init(), 0, 0, 0,
+                            neg_inf(), neg_inf(), false};
+    stream_ranges_warps<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -702,12 +1201,18 @@ cudaError_t launch_sample_t(const StreamGeom& g, const SampleDev& p, cudaStream_
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(sample_stream_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kSampDynSmem));
+        cudaError_t e = cudaFuncSetAttribute(sample_stream_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kWarpDynSmem));
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(sample_wide_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kWideDynSmem));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    sample_stream_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kSampDynSmem, stream>>>(g, p);
+    if (p.k <= kWarpMaxK)
+        sample_stream_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kWarpDynSmem, stream>>>(g, p);
+    else
+        sample_wide_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kWideDynSmem, stream>>>(g, p);
     return cudaGetLastError();
 }
 

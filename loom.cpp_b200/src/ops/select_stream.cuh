@@ -114,6 +114,7 @@ struct StreamCtl {
     int abort;
     int issued;
     int consumed;
+    int waited[16];  // stream_ranges_warps: stages each consumer warp saw land
 };
 
 // The persistent CTA body. Consumers are warps [0, kConsumerWarps); warp kConsumerWarps produces.
@@ -218,6 +219,151 @@ __device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, S
     // Drain: every bulk copy issued must have landed before the CTA's shared memory goes away.
     if (threadIdx.x == 0) {
         for (int i = ctl->consumed; i < ctl->issued; ++i) {
+            if (!mbar_wait_bounded(&ctl->full[i % kStages], (i / kStages) & 1, status)) break;
+        }
+    }
+    __syncthreads();
+}
+
+// Waits, as a whole warp, for the phase of `bar` with the given parity: every lane polls the barrier
+// (so each lane has the barrier's acquire), lane 0's clock and the abort flag decide for the warp.
+// False when the wait runs out (recorded as LOOM_SELECT_ETIMEOUT) or another warp has aborted.
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word, const int* abort) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (__all_sync(0xffffffffu, mbar_try_wait_sleep(bar, parity))) return true;
+        int give_up = 0;
+        if ((threadIdx.x & 31) == 0) {
+            if (*reinterpret_cast<const volatile int*>(abort)) give_up = 1;
+            else if (global_timer_ns() - t0 > kWaitLimitNs) give_up = 2;
+        }
+        give_up = __shfl_sync(0xffffffffu, give_up, 0);
+        if (give_up) {
+            if (give_up == 2 && (threadIdx.x & 31) == 0) record_status(status_word, LOOM_SELECT_ETIMEOUT);
+            return false;
+        }
+    }
+}
+
+// mbar_wait_bounded for one thread that also gives up once another warp has aborted.
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int* status_word, const int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (*reinterpret_cast<const volatile int*>(abort)) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_status(status_word, LOOM_SELECT_ETIMEOUT);
+            return false;
+        }
+    }
+}
+
+// The persistent CTA body with free-running consumer warps: each consumer warp waits for a stage
+// and releases it by itself, so warps drift apart (by up to kStages stages) instead of meeting at a
+// barrier every stage. The only CTA-wide barriers are the op's own, in begin_segment, in the first
+// chunk of a segment and in end_segment; every consumer warp makes the same sequence of calls.
+// A warp whose wait gives up raises the abort flag and goes on "dead": it no longer waits, reads or
+// releases stages, but still makes every op call (chunk with live == false), so the op's barriers
+// still match; the producer and the other warps see the flag and wind down the same way.
+// Op hooks, all called by every consumer thread:
+//   op.begin_segment(seg)
+//   op.chunk(seg, data, col0, n, live)         live == false: touch no stage data
+//   op.end_segment(seg)
+template <int kStages, int kStageBytes, int kConsumerWarps, class Op>
+__device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* ring, StreamCtl* ctl, int* status) {
+    static_assert(kStages <= 16 && kConsumerWarps <= 16, "control block sizes");
+    static_assert(kStageBytes % 16 == 0, "stage must be a multiple of 16 bytes");
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t c = blockIdx.x;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&ctl->full[i], 1);
+            mbar_init(&ctl->empty[i], kConsumerWarps);
+        }
+        ctl->abort = 0;
+        ctl->issued = 0;
+        ctl->consumed = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    const int64_t lo = split_point(g, c), hi = split_point(g, c + 1);
+    const int64_t row_first = lo / g.width;
+    const int64_t row_last = hi > lo ? (hi - 1) / g.width : row_first - 1;
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer (as in stream_ranges, with abortable waits) ----------------
+        int it = 0;
+        bool stop = false;
+        for (int64_t r = row_first; r <= row_last && !stop; ++r) {
+            const Segment s = make_segment<kStageBytes>(g, c, r);
+            for (int32_t k = 0; k < s.n_chunks; ++k) {
+                const int slot = it % kStages;
+                const uint32_t parity = ((it / kStages) & 1) ^ 1;
+                int ok = 1;
+                if (lane == 0) {
+                    ok = mbar_wait_abortable(&ctl->empty[slot], parity, status, &ctl->abort) ? 1 : 0;
+                    if (!ok) atomicExch(&ctl->abort, 1);
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    stop = true;
+                    break;
+                }
+                if (lane == 0) {
+                    const unsigned char* src = s.A0 + static_cast<int64_t>(k) * kStageBytes;
+                    const int64_t left = s.A1 - src;
+                    const uint32_t bytes = static_cast<uint32_t>(left < kStageBytes ? left : kStageBytes);
+                    mbar_arrive_expect_tx(&ctl->full[slot], bytes);
+                    bulk_g2s(ring + static_cast<size_t>(slot) * kStageBytes, src, bytes, &ctl->full[slot]);
+                }
+                __syncwarp();
+                ++it;
+            }
+        }
+        if (lane == 0) ctl->issued = it;
+    } else {
+        // ---------------- consumers: one warp at a time ----------------
+        int it = 0, waited = 0;
+        bool live = true;
+        for (int64_t r = row_first; r <= row_last; ++r) {
+            const Segment s = make_segment<kStageBytes>(g, c, r);
+            op.begin_segment(s);
+            for (int32_t k = 0; k < s.n_chunks; ++k) {
+                const int slot = it % kStages;
+                const uint32_t parity = (it / kStages) & 1;
+                if (live) {
+                    live = warp_wait_bounded(&ctl->full[slot], parity, status, &ctl->abort);
+                    if (live) waited = it + 1;
+                    else if (lane == 0) atomicExch(&ctl->abort, 1);
+                }
+                const unsigned char* src = s.A0 + static_cast<int64_t>(k) * kStageBytes;
+                const int64_t left = s.A1 - src;
+                const int32_t bytes = static_cast<int32_t>(left < kStageBytes ? left : kStageBytes);
+                const int64_t col0 = s.j0 + (src - s.a0) / g.esz;
+                op.chunk(s, ring + static_cast<size_t>(slot) * kStageBytes, col0, bytes / g.esz, live);
+                if (live) {
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->empty[slot]);
+                }
+                ++it;
+            }
+            op.end_segment(s);
+        }
+        if (lane == 0) ctl->waited[warp] = waited;
+    }
+    __syncthreads();
+    // Drain: every bulk copy issued must have landed before the CTA's shared memory goes away. The
+    // copies not yet seen by every warp are the last (at most kStages) issued ones.
+    if (threadIdx.x == 0) {
+        int from = ctl->issued;
+        for (int w = 0; w < kConsumerWarps; ++w) from = ctl->waited[w] < from ? ctl->waited[w] : from;
+        for (int i = from; i < ctl->issued; ++i) {
             if (!mbar_wait_bounded(&ctl->full[i % kStages], (i / kStages) & 1, status)) break;
         }
     }
