@@ -321,10 +321,16 @@ __device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row,
     group_sync<kNT>();
 }
 
+template <int kNT, int kCap, bool kSmallK>
+__device__ __forceinline__ int select_best(uint64_t* cand, int n, int k, TopkShared* sh) {
+    if constexpr (kSmallK) return topk_select_sorted_small_k<kNT, kCap>(cand, n, k, sh);
+    else return topk_select_sorted<kNT, kCap>(cand, n, k, sh);
+}
+
 // The end of a row segment, once its K best keys are sorted in cand[0, K): a whole row is finalised
 // here; a piece of a split row writes its record and takes the row's ticket, and the CTA that takes
 // the last ticket merges every piece's record and finalises the row. cand holds kCap keys.
-template <int kDtype, int kNT, int kCap>
+template <int kDtype, int kNT, int kCap, bool kSmallK>
 __device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segment& s, uint64_t* cand, double* e,
                                double* S, int K, LseAcc seg, bool bad, SampleShared* sh) {
     const int tid = threadIdx.x;
@@ -367,13 +373,13 @@ __device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segm
         part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
         part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
         tot = lse_merge(tot, part);
-        if (have + c > kCap) have = topk_select_sorted<kNT, kCap>(cand, have, p.k, &sh->tk);
+        if (have + c > kCap) have = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
         const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
         for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
         have += c;
         group_sync<kNT>();
     }
-    const int Kf = topk_select_sorted<kNT, kCap>(cand, have, p.k, &sh->tk);
+    const int Kf = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
     if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
     finalize_row<kDtype, kNT>(p, g, s.row, cand, e, S, Kf, tot, any_bad, sh);
 }
@@ -607,7 +613,7 @@ struct WideSampleOp {
             sh->seg_lse = a;
         }
         prune<kNT>(p, cand, slots, hset, qn, sh);  // also syncs
-        finish_segment<kDtype, kNT, kCandCap>(p, g, s, cand, reinterpret_cast<double*>(cand + kDecideSlots), S, sh->K,
+        finish_segment<kDtype, kNT, kCandCap, false>(p, g, s, cand, reinterpret_cast<double*>(cand + kDecideSlots), S, sh->K,
                                              sh->seg_lse, sh->bad != 0, sh);
     }
 };
@@ -640,11 +646,13 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
 // is full the warp alone tempers it into rank keys, keeps its best k (a register bitonic sort) and
 // raises the CTA's thresholds with shared-memory atomics: key_t, which every kept key reaches, and X,
 // the raw bound derived from it. Both only rise, so a warp that reads them late keeps more than it
-// needs, never less. What raises them in the common case costs one max per vector: every lane keeps
-// the running maximum of the non-history elements it has read in the segment; after a stage a warp
-// publishes the ceil(k / warps)-th largest of its 32 lanes' maxima, and the smallest published value
-// is reached by at least k distinct elements (the lanes' element sets are disjoint), so it bounds the
-// k-th best from below. The stream skips history ids' raw values (a hash lookup, only for elements
+// needs, never less. What raises them in the common case costs one max per vector: each warp keeps,
+// one per lane, a sorted list of the 32 largest "stage maxima" it has seen in the segment (the
+// maximum of one lane's elements in one stage: distinct elements, taken at their true, penalised
+// value when they are history ids); a lane whose stage maximum beats the list's ceil(k / warps)-th
+// entry inserts it (a shuffle and a select). That entry, published now and then, is reached by
+// ceil(k / warps) distinct elements of the warp, so the smallest value the warps have published is
+// reached by at least k and bounds the k-th best from below. The stream skips history ids' raw values (a hash lookup, only for elements
 // that pass X); at the segment end the CTA reads their logits again from global memory (the row has
 // just gone through L2), penalises and tempers them, and offers them against the final threshold.
 // A segment ends with every warp's best k merged by the whole CTA (exact selection, then the
@@ -655,6 +663,7 @@ constexpr int kRawCap = 128;                      // raw pairs a warp holds betw
 constexpr int kWarpKeyCap = kWarpMaxK + kRawCap;  // a warp's kept keys plus one tempered raw batch
 constexpr int kWarpCand = kSampWarps * kRawCap;   // the segment-end gather (aliases the raw buffers)
 static_assert(kSampWarps * kWarpMaxK <= kWarpCand, "the warps' best k keys fit the gather");
+static_assert(kWarpMaxK <= kSampNT, "the warp path ranks at most one key per thread");
 static_assert(kWarpKeyCap <= 256, "a warp sorts at most 8 keys per lane");
 static_assert(2 * kWarpMaxK * sizeof(double) <= kSampWarps * kWarpKeyCap * sizeof(uint64_t),
               "decision scratch fits the key buffers");
@@ -760,9 +769,9 @@ struct WarpSampleOp {
     int nr;      // raw pairs this warp holds (the same in every lane)
     int nk;      // keys this warp keeps
     int stage;   // stage index within the segment
-    float rmax;    // this lane's running maximum over the non-history elements it has read
-    float wv;      // this warp's published value (sh->wq[warp])
-    bool crossed;  // rmax has risen above wv since the last publish
+    float tv;      // this lane's entry of the warp's sorted list of stage maxima (lane i: i-th largest)
+    float wv;      // the list's ceil(k / warps)-th entry
+    bool pending;  // wv has risen since it was last published
 
     __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
     __device__ const int32_t* row_hist(int64_t row) const { return p.hist + row * static_cast<int64_t>(p.hist_len); }
@@ -790,22 +799,35 @@ struct WarpSampleOp {
         if (floor > old) atomicMax(&sh->x_key, loom_order_key(inverse_threshold_bound(t, p.T, p.greedy)));
     }
 
-    // Warp-collective: when a lane's maximum has crossed the published value since the last call
-    // (`crossed`), publishes this warp's
-    // ceil(k / warps)-th largest lane maximum and raises the thresholds to the smallest value the
-    // warps have published. (Only a crossing can change that order statistic.)
+    // Warp-collective: inserts every lane's value c with `take` into the warp's sorted list, and
+    // updates wv.
+    __device__ __forceinline__ void list_insert(bool take, float c) {
+        const int lane = threadIdx.x & 31;
+        uint32_t b = __ballot_sync(0xffffffffu, take);
+        while (b) {
+            const int src = __ffs(b) - 1;
+            b &= b - 1u;
+            const float ci = __shfl_sync(0xffffffffu, c, src);
+            const float up = __shfl_up_sync(0xffffffffu, tv, 1);  // lane i: entry i - 1
+            if (!(tv >= ci)) tv = (lane == 0 || up >= ci) ? ci : up;
+        }
+        const float v = __shfl_sync(0xffffffffu, tv, (p.k + kSampWarps - 1) / kSampWarps - 1);
+        if (v > wv) {
+            wv = v;
+            pending = true;
+        }
+    }
+
+    // Warp-collective: publishes wv when it has risen and raises the thresholds to the smallest
+    // value the warps have published.
     __device__ void publish() {
+        if (!pending) return;
+        pending = false;
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-        if (!__any_sync(0xffffffffu, crossed)) return;
-        crossed = false;
-        const float sorted = warp_sort_desc(rmax);
-        const float v = __shfl_sync(0xffffffffu, sorted, (p.k + kSampWarps - 1) / kSampWarps - 1);
-        if (!(v > wv)) return;
-        wv = v;
         if (lane == 0) {
             volatile float* wq = sh->wq;
-            wq[warp] = v;
-            float mn = v;
+            wq[warp] = wv;
+            float mn = wv;
             for (int w = 0; w < kSampWarps; ++w) mn = fminf(mn, wq[w]);
             raise_raw(mn);
         }
@@ -866,9 +888,9 @@ struct WarpSampleOp {
         nr = 0;
         nk = 0;
         stage = 0;
-        rmax = neg_inf();
+        tv = neg_inf();
         wv = neg_inf();
-        crossed = false;
+        pending = false;
         if (p.penalty) {
             int4* h4 = reinterpret_cast<int4*>(hset);
             for (int i = tid; i < kHashSlots / 4; i += kNT) h4[i] = make_int4(-1, -1, -1, -1);
@@ -922,8 +944,8 @@ struct WarpSampleOp {
             }
             if (at >= 0 && is_history(at)) m = neg_inf();
         }
-        rmax = m;
         const float sorted = warp_sort_desc(m);
+        tv = sorted;  // the list starts as the first stage's lane maxima
         const int q = (p.k + kSampWarps - 1) / kSampWarps;  // <= 16
         const float bw = __shfl_sync(0xffffffffu, sorted, q - 1);
         wv = bw;
@@ -991,12 +1013,11 @@ struct WarpSampleOp {
             for (int i = 0; i < kVecsPerThread; ++i) hits |= static_cast<uint32_t>(mu[i] >= X) << i;
         }
 
-        // The running maximum. Values at or below the published wv never decide the published order
-        // statistic (it only rises), so only a rise above wv must be a non-history element's value:
-        // that rare case finds the vector holding the maximum (from mu[]) and skips the rise when the
-        // maximum there is a history id's raw value.
-        if (smax > rmax) {
-            bool ok = true;
+        // The warp's list of stage maxima (the first stage's are already in it, from the warm-up).
+        // A lane whose maximum beats wv finds the vector holding it (from mu[]) and, with a
+        // penalty, checks whether that element is a history id: then it enters at its penalised value.
+        if (st > 0 && __any_sync(0xffffffffu, smax > wv)) {
+            float c = smax;
             if (p.penalty && smax > wv) {
                 int at = 0;
 #pragma unroll
@@ -1005,15 +1026,13 @@ struct WarpSampleOp {
                 const int32_t v = at * kNT + tid;
                 Vec16<kDtype> e;
                 e.unpack(v4[v]);
-                ok = false;
+                int q = 0;
 #pragma unroll
-                for (int q = 0; q < kPer; ++q)
-                    if (e.x[q] == smax && !is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) ok = true;
+                for (int t = kPer - 1; t >= 0; --t)
+                    if (e.x[t] == smax) q = t;
+                if (is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) c = penalise(smax, p.r);
             }
-            if (ok) {
-                crossed = crossed || (rmax <= wv && smax > wv);
-                rmax = smax;
-            }
+            list_insert(c > wv, c);
         }
         if (st < 4 || (st & 3) == 3) publish();  // every stage at first, then every fourth at most
 
@@ -1092,9 +1111,9 @@ struct WarpSampleOp {
             sh->seg_lse = a;
         }
         group_sync<kNT>();
-        const int K = topk_select_sorted<kNT, kWarpCand>(cand, sh->K, p.k, &sh->tk);
+        const int K = topk_select_sorted_small_k<kNT, kWarpCand>(cand, sh->K, p.k, &sh->tk);
         double* e = reinterpret_cast<double*>(keys0);
-        finish_segment<kDtype, kNT, kWarpCand>(p, g, s, cand, e, e + kWarpMaxK, K, sh->seg_lse, sh->bad != 0, sh);
+        finish_segment<kDtype, kNT, kWarpCand, true>(p, g, s, cand, e, e + kWarpMaxK, K, sh->seg_lse, sh->bad != 0, sh);
     }
 };
 
@@ -1117,7 +1136,7 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
     const int w = warp < kSampWarps ? warp : 0;  // the producer warp holds no buffers
     WarpSampleOp<kDtype> op{g,     p,    &sh,  raw_all + w * kRawCap, keys_all + w * kWarpKeyCap,
                             reinterpret_cast<uint64_t*>(raw_all), keys_all, hset, uniq, lse_init(), 0, 0, 0,
-                            neg_inf(), neg_inf(), false};
+                            neg_inf(), neg_inf(), false};  // (tv, wv, pending)
     stream_ranges_warps<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 

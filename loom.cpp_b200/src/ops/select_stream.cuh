@@ -61,19 +61,26 @@ struct Segment {
     int32_t n_chunks;
 };
 
+// Segment of range c in `row`; lo and hi are the range's bounds (split_point(g, c), split_point(g, c + 1)).
+// A row that starts at or after lo and ends at or before hi lies wholly in the range (no search).
 template <int kStageBytes>
-__device__ __forceinline__ Segment make_segment(const StreamGeom& g, int64_t c, int64_t row) {
+__device__ __forceinline__ Segment make_segment(const StreamGeom& g, int64_t c, int64_t row, int64_t lo, int64_t hi) {
     Segment s;
-    const int64_t lo = split_point(g, c), hi = split_point(g, c + 1);
     const int64_t rs = row * g.width;
     s.row = row;
     s.j0 = (lo > rs ? lo : rs) - rs;
     s.j1 = (hi < rs + g.width ? hi : rs + g.width) - rs;
-    const int64_t c0 = range_of(g, rs);
-    const int64_t c1 = range_of(g, rs + g.width - 1);
-    s.index = static_cast<int32_t>(c - c0);
-    s.count = static_cast<int32_t>(c1 - c0 + 1);
-    s.first_cta = c0;
+    if (rs >= lo && rs + g.width <= hi) {
+        s.index = 0;
+        s.count = 1;
+        s.first_cta = c;
+    } else {
+        const int64_t c0 = range_of(g, rs);
+        const int64_t c1 = range_of(g, rs + g.width - 1);
+        s.index = static_cast<int32_t>(c - c0);
+        s.count = static_cast<int32_t>(c1 - c0 + 1);
+        s.first_cta = c0;
+    }
     const unsigned char* rowp = g.base + row * g.row_stride * g.esz;
     s.a0 = rowp + s.j0 * g.esz;
     s.a1 = rowp + s.j1 * g.esz;
@@ -155,7 +162,7 @@ __device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, S
         int it = 0;
         bool stop = false;
         for (int64_t r = row_first; r <= row_last && !stop; ++r) {
-            const Segment s = make_segment<kStageBytes>(g, c, r);
+            const Segment s = make_segment<kStageBytes>(g, c, r, lo, hi);
             for (int32_t k = 0; k < s.n_chunks; ++k) {
                 const int slot = it % kStages;
                 const uint32_t parity = ((it / kStages) & 1) ^ 1;
@@ -187,7 +194,7 @@ __device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, S
         int it = 0;
         bool stop = false;
         for (int64_t r = row_first; r <= row_last && !stop; ++r) {
-            const Segment s = make_segment<kStageBytes>(g, c, r);
+            const Segment s = make_segment<kStageBytes>(g, c, r, lo, hi);
             op.begin_segment(s);
             for (int32_t k = 0; k < s.n_chunks; ++k) {
                 const int slot = it % kStages;
@@ -202,8 +209,9 @@ __device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, S
                 const unsigned char* src = s.A0 + static_cast<int64_t>(k) * kStageBytes;
                 const int64_t left = s.A1 - src;
                 const int32_t bytes = static_cast<int32_t>(left < kStageBytes ? left : kStageBytes);
-                const int64_t col0 = s.j0 + (src - s.a0) / g.esz;
-                op.chunk(s, ring + static_cast<size_t>(slot) * kStageBytes, col0, bytes / g.esz);
+                const int esz_log2 = g.esz == 4 ? 2 : 1;  // 4-byte or 2-byte elements
+                const int64_t col0 = s.j0 + ((src - s.a0) >> esz_log2);
+                op.chunk(s, ring + static_cast<size_t>(slot) * kStageBytes, col0, bytes >> esz_log2);
                 op.end_chunk(s);
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -300,7 +308,7 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
         int it = 0;
         bool stop = false;
         for (int64_t r = row_first; r <= row_last && !stop; ++r) {
-            const Segment s = make_segment<kStageBytes>(g, c, r);
+            const Segment s = make_segment<kStageBytes>(g, c, r, lo, hi);
             for (int32_t k = 0; k < s.n_chunks; ++k) {
                 const int slot = it % kStages;
                 const uint32_t parity = ((it / kStages) & 1) ^ 1;
@@ -331,7 +339,7 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
         int it = 0, waited = 0;
         bool live = true;
         for (int64_t r = row_first; r <= row_last; ++r) {
-            const Segment s = make_segment<kStageBytes>(g, c, r);
+            const Segment s = make_segment<kStageBytes>(g, c, r, lo, hi);
             op.begin_segment(s);
             for (int32_t k = 0; k < s.n_chunks; ++k) {
                 const int slot = it % kStages;
@@ -344,8 +352,9 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
                 const unsigned char* src = s.A0 + static_cast<int64_t>(k) * kStageBytes;
                 const int64_t left = s.A1 - src;
                 const int32_t bytes = static_cast<int32_t>(left < kStageBytes ? left : kStageBytes);
-                const int64_t col0 = s.j0 + (src - s.a0) / g.esz;
-                op.chunk(s, ring + static_cast<size_t>(slot) * kStageBytes, col0, bytes / g.esz, live);
+                const int esz_log2 = g.esz == 4 ? 2 : 1;  // 4-byte or 2-byte elements
+                const int64_t col0 = s.j0 + ((src - s.a0) >> esz_log2);
+                op.chunk(s, ring + static_cast<size_t>(slot) * kStageBytes, col0, bytes >> esz_log2, live);
                 if (live) {
                     fence_proxy_async_smem();
                     __syncwarp();

@@ -20,6 +20,12 @@ struct TopkShared {
     uint64_t prefix;
 };
 
+__device__ __forceinline__ int next_pow2(int n) {
+    int p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+
 // Radix select: finds the rule that keeps exactly K = min(k, n) of the n keys -- those with
 // (key >> shift) >= (prefix >> shift) -- and compacts them to cand[0, K) (in no particular order).
 // Keys are distinct (ids are), so the K kept are exactly the K largest.
@@ -169,20 +175,28 @@ __device__ int topk_rank_sort(uint64_t* cand, int n, int k) {
 }
 
 // The K = min(k, n) largest keys of cand[0, n), sorted descending, in cand[0, K). Large sets are
-// first cut to k by the radix select, then ranked. n <= kCap (the buffer), k <= 1024.
+// first cut to k by the radix select; up to kNT keys are then ranked (O(n^2 / kNT) compares, one
+// barrier), more are sorted by the bitonic network (O(n log^2 n / kNT), a barrier per pass).
+// n <= kCap (the buffer), k <= 1024; cand has room for 1024 keys.
+// The same for k <= kNT: a radix cut (when n > 2 kNT), then the ranking.
 template <int kNT, int kCap>
-__device__ int topk_select_sorted(uint64_t* cand, int n, int k, TopkShared* sh) {
+__device__ int topk_select_sorted_small_k(uint64_t* cand, int n, int k, TopkShared* sh) {
     if (n > 2 * kNT) n = topk_select_compact<kNT, (kCap + kNT - 1) / kNT>(cand, n, k, sh);
     if (n <= kNT) return topk_rank_sort<kNT, 1>(cand, n, k);
-    if (n <= 2 * kNT) return topk_rank_sort<kNT, 2>(cand, n, k);
-    return topk_rank_sort<kNT, (1024 + kNT - 1) / kNT>(cand, n, k);
+    return topk_rank_sort<kNT, 2>(cand, n, k);
 }
 
-__device__ __forceinline__ int next_pow2(int n) {
-    int p = 1;
-    while (p < n) p <<= 1;
-    return p;
+template <int kNT, int kCap>
+__device__ int topk_select_sorted(uint64_t* cand, int n, int k, TopkShared* sh) {
+    static_assert(kCap >= 1024, "the bitonic sort of up to 1024 keys works in place");
+    if (n > 2 * kNT) n = topk_select_compact<kNT, (kCap + kNT - 1) / kNT>(cand, n, k, sh);
+    if (n <= kNT) return topk_rank_sort<kNT, 1>(cand, n, k);
+    if (n > k) n = topk_select_compact<kNT, (kCap + kNT - 1) / kNT>(cand, n, k, sh);
+    if (n <= kNT) return topk_rank_sort<kNT, 1>(cand, n, k);
+    topk_sort_desc<kNT>(cand, n, next_pow2(n));
+    return n;
 }
+
 
 // Monotone map of non-NaN floats to int32 (distinguishes -0 < +0), and back.
 __device__ __forceinline__ int32_t float_to_ordinal(float x) {
