@@ -46,8 +46,9 @@ struct ArgmaxOp {
     // Steps of kU vectors per thread, columns increasing from step to step. A step can change the
     // warp's best only where some element reaches it (or, before anything is taken, equals -inf);
     // then the lanes' own bests join the warp's in one reduction (value desc, column asc).
-    __device__ void chunk(const Segment&, const unsigned char* data, int64_t col0, int32_t n) {
+    __device__ void chunk(const Segment&, const unsigned char* data, int64_t col0, int32_t n, bool live) {
         constexpr int kNT = kArgNT;
+        if (!live) return;
         const int32_t nvec = n / kPer;
         const uint4* v4 = reinterpret_cast<const uint4*>(data);
         const int32_t nsteps = (nvec + kU * kNT - 1) / (kU * kNT);
@@ -84,8 +85,6 @@ struct ArgmaxOp {
             }
         }
     }
-
-    __device__ void end_chunk(const Segment&) {}
 
     // The loom.cpp rule on the row's final (value, column): a NaN in column 0 wins.
     __device__ int32_t final_col(int64_t row, ArgBest b) const {
@@ -142,7 +141,7 @@ __global__ void __launch_bounds__((kArgWarps + 1) * 32, 1)
     __shared__ StreamCtl ctl;
     __shared__ ArgShared sh;
     ArgmaxOp<kDtype> op{g, lo, out_ids, records, tickets, &sh, arg_init()};
-    stream_ranges<kArgStages, kArgStageBytes, kArgWarps>(g, op, ring, &ctl, status);
+    stream_ranges_warps<kArgStages, kArgStageBytes, kArgWarps>(g, op, ring, &ctl, status);
 }
 
 template <int kDtype>

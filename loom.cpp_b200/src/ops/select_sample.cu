@@ -658,6 +658,8 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
 // A segment ends with every warp's best k merged by the whole CTA (exact selection, then the
 // decision).
 
+constexpr int kWarpStages = 2;                    // the warp path's ring
+constexpr int kWarpStageBytes = 36864;  // 9 vectors per thread; two CTAs per SM leave no room for more
 constexpr int kWarpMaxK = 128;                    // the warp path serves top_k up to this
 constexpr int kRawCap = 128;                      // raw pairs a warp holds between its prunes
 constexpr int kWarpKeyCap = kWarpMaxK + kRawCap;  // a warp's kept keys plus one tempered raw batch
@@ -977,7 +979,7 @@ struct WarpSampleOp {
         // 2. mark. The common path is one max per element: each vector's maximum mu[i] (NaN for a
         //    vector past the stage's end) and the lane's stage maximum smax; only a lane whose smax
         //    reaches X (rare) turns its mu[i] into marks.
-        constexpr int kVecsPerThread = kSampStageBytes / 16 / kNT;
+        constexpr int kVecsPerThread = kWarpStageBytes / 16 / kNT;
         static_assert(kVecsPerThread <= 32, "marks are one 32-bit word");
         float mu[kVecsPerThread];
         float smax = neg_inf();
@@ -1117,7 +1119,7 @@ struct WarpSampleOp {
     }
 };
 
-constexpr size_t kWarpDynSmem = static_cast<size_t>(kSampStages) * kSampStageBytes +
+constexpr size_t kWarpDynSmem = static_cast<size_t>(kWarpStages) * kWarpStageBytes +
                                 kSampWarps * kRawCap * sizeof(uint2) + kSampWarps * kWarpKeyCap * sizeof(uint64_t) +
                                 kHashSlots * sizeof(int32_t) + kMaxHistory * sizeof(int32_t);
 static_assert(kWarpDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
@@ -1128,7 +1130,7 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
     __shared__ StreamCtl ctl;
     __shared__ SampleShared sh;
     unsigned char* ring = dyn;
-    uint2* raw_all = reinterpret_cast<uint2*>(dyn + static_cast<size_t>(kSampStages) * kSampStageBytes);
+    uint2* raw_all = reinterpret_cast<uint2*>(dyn + static_cast<size_t>(kWarpStages) * kWarpStageBytes);
     uint64_t* keys_all = reinterpret_cast<uint64_t*>(raw_all + kSampWarps * kRawCap);
     int32_t* hset = reinterpret_cast<int32_t*>(keys_all + kSampWarps * kWarpKeyCap);
     int32_t* uniq = hset + kHashSlots;
@@ -1137,7 +1139,7 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
     WarpSampleOp<kDtype> op{g,     p,    &sh,  raw_all + w * kRawCap, keys_all + w * kWarpKeyCap,
                             reinterpret_cast<uint64_t*>(raw_all), keys_all, hset, uniq, lse_init(), 0, 0, 0,
                             neg_inf(), neg_inf(), false};  // (tv, wv, pending)
-    stream_ranges_warps<kSampStages, kSampStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
+    stream_ranges_warps<kWarpStages, kWarpStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 
 // ---------------------------------------------------------------------------------------------
