@@ -244,18 +244,24 @@ def workload_shard(sel, synth, torch, dev, rank):
 WORKLOADS = {"sample": workload_sample, "greedy": workload_greedy, "ctc": workload_ctc, "shard": workload_shard}
 
 
-def cpu_baseline_sample(synth, torch, nthreads, rows=1024):
-    """The oracle's sampling chain on `rows` host rows with all host threads (a bounded sample)."""
+def cpu_baseline_sample(synth, torch, nthreads, rows=1024, min_seconds=10.0):
+    """The oracle's sampling chain on the [rows, V] host batch with all host threads, repeated until
+    at least `min_seconds` of CPU time have passed (a bounded sample). Returns (rows/s, seconds, passes)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_binding as ob
 
     x, hist, u = synth.sample_chain(rows, seed=2, device="cpu")
     xn, hn, un = x.numpy(), hist.numpy(), u.numpy()
     ob.sample_rows(xn[:8], un[:8], T, R, K, P, hn[:8], want_logp=False, nthreads=nthreads)  # warm
+    passes = 0
     t0 = time.perf_counter()
-    ob.sample_rows(xn, un, T, R, K, P, hn, want_logp=False, nthreads=nthreads)
-    dt = time.perf_counter() - t0
-    return rows / dt, dt
+    while True:
+        ob.sample_rows(xn, un, T, R, K, P, hn, want_logp=False, nthreads=nthreads)
+        passes += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return rows * passes / dt, dt, passes
 
 
 def run_reference(args):
@@ -367,9 +373,10 @@ def run_b200(args):
         line["e2e"] = e2e_obj
     if rank == 0 and world == 1 and args.workload == "sample" and not args.no_cpu_baseline:
         nthreads = os.cpu_count() or 1
-        v, dt = cpu_baseline_sample(synth, torch, nthreads)
+        v, dt, passes = cpu_baseline_sample(synth, torch, nthreads)
         line["cpu_baseline"] = {"value": v, "unit": "rows/s", "cores": nthreads, "kind": "port",
-                                "sample": f"1024 rows of the same workload once ({dt:.1f} s), host memory"}
+                                "sample": f"the [1024, {VOCAB}] f32 batch of the same workload, {passes} passes "
+                                          f"({dt:.1f} s), host memory"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -54,7 +54,6 @@ struct CtcShared {
     int64_t last_utt[kMaxUttPerCta];
     int last_ticket[kMaxUttPerCta]; // -1: the utterance lies wholly in this CTA
     int warp_tot[kRowWarps];
-    int carry;
 };
 
 // Frames are split evenly: CTA c owns [c * total / G, (c + 1) * total / G).
@@ -68,40 +67,54 @@ __device__ __forceinline__ int64_t ctc_cta_of_frame(int64_t f, int64_t total, in
     return c;
 }
 
-// Compacts utterance u's kept frames. Called by the whole CTA.
+// Compacts utterance u's kept frames. Called by the whole CTA. Each thread takes kCollapsePer
+// consecutive frames (their ids loaded at once), and one block scan per pass places the kept ones.
+constexpr int kCollapsePer = 8;
+
 __device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const int32_t* frame_ids, int32_t* out_ids,
                              int32_t* out_frames, int32_t* out_len, CtcShared* sh) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int32_t* ids = frame_ids + u * n_frames;
-    if (threadIdx.x == 0) sh->carry = 0;
-    __syncthreads();
-    for (int64_t base = 0; base < n_frames; base += kRowNT) {
-        const int64_t f = base + threadIdx.x;
-        int32_t id = 0;
-        bool keep = false;
-        if (f < n_frames) {
-            id = __ldcg(ids + f);
-            const int32_t prev = f == 0 ? blank : __ldcg(ids + f - 1);
-            keep = id != prev && id != blank;
+    int carry = 0;  // frames kept by the earlier passes (the same in every thread)
+    for (int64_t base = 0; base < n_frames; base += static_cast<int64_t>(kRowNT) * kCollapsePer) {
+        const int64_t f0 = base + static_cast<int64_t>(threadIdx.x) * kCollapsePer;
+        int32_t v[kCollapsePer];
+        const int32_t prev0 = (f0 == 0 || f0 > n_frames) ? blank : __ldcg(ids + f0 - 1);
+#pragma unroll
+        for (int j = 0; j < kCollapsePer; ++j) v[j] = f0 + j < n_frames ? __ldcg(ids + f0 + j) : blank;
+        uint32_t keep = 0;
+#pragma unroll
+        for (int j = 0; j < kCollapsePer; ++j) {
+            const int32_t prev = j == 0 ? prev0 : v[j - 1];
+            keep |= static_cast<uint32_t>(f0 + j < n_frames && v[j] != prev && v[j] != blank) << j;
         }
-        const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0) sh->warp_tot[warp] = __popc(ballot);
-        __syncthreads();
-        int before = sh->carry;
-        for (int w = 0; w < warp; ++w) before += sh->warp_tot[w];
-        int total = 0;
-        for (int w = 0; w < kRowWarps; ++w) total += sh->warp_tot[w];
-        if (keep) {
-            const int pos = before + __popc(ballot & ((1u << lane) - 1u));
-            out_ids[u * n_frames + pos] = id;
-            out_frames[u * n_frames + pos] = static_cast<int32_t>(f);
+        const int cnt = __popc(keep);
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
         }
+        if (lane == 31) sh->warp_tot[warp] = incl;
         __syncthreads();
-        if (threadIdx.x == 0) sh->carry += total;
-        __syncthreads();
+        int pos = carry + incl - cnt, total = 0;
+        for (int w = 0; w < kRowWarps; ++w) {
+            const int t = sh->warp_tot[w];
+            if (w < warp) pos += t;
+            total += t;
+        }
+#pragma unroll
+        for (int j = 0; j < kCollapsePer; ++j) {
+            if ((keep >> j) & 1u) {
+                out_ids[u * n_frames + pos] = v[j];
+                out_frames[u * n_frames + pos] = static_cast<int32_t>(f0 + j);
+                ++pos;
+            }
+        }
+        carry += total;
+        __syncthreads();  // warp_tot is rewritten by the next pass
     }
-    if (threadIdx.x == 0) out_len[u] = sh->carry;
-    __syncthreads();
+    if (threadIdx.x == 0) out_len[u] = carry;
 }
 
 template <int kDtype, bool kLogp>

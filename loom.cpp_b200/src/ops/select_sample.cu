@@ -1,25 +1,24 @@
 // select_sample.cu -- the fused sampling chain (K2) and the vocabulary-shard merge (K4).
 //
-// One pass over the logits: rows stream through shared memory (select_stream.cuh). The per-element
-// work is a compare without branches: each thread marks, in a register bitmask, which of its
-// vectors of the stage (16 bytes each) have a maximum reaching a threshold X. Every element below X
-// is strictly worse than k elements already kept (X is at most the smallest raw value whose tempered
-// value x / T reaches the current k-th best). At the end of the stage each thread sweeps its few
-// marked vectors: the elements that pass go, raw, into the thread's own slots in shared memory (one
-// store each; no atomics, no shuffles, no divides).
+// One pass over the logits: rows stream through shared memory, and every element below a threshold
+// X is dropped with one compare (X is at most the smallest raw value whose tempered value x / T
+// reaches a lower bound of the row's k-th best, so no element of the top-k is ever below it). The few
+// elements that reach X become candidates; at the end of a row segment the exact top-k of the
+// candidates is ranked into order and the survivor decision runs in double precision on one warp
+// (select_topk.cuh), in exactly the oracle's operation order.
 //
-// At the end of a stage, when more than k + kPruneSlack candidates are held, they are tempered with
-// an IEEE divide (in parallel), the exact top-k is kept as 64-bit rank keys, and X rises to the k-th.
-// The first stage of each row segment seeds X: each warp sorts its lanes' maxima and the smallest of
-// the warps' ceil(k / warps)-th largest is a value that at least k elements reach.
+// Two kernels share the row-segment bookkeeping (records and tickets of split rows, the decision):
+//   sample_stream_kernel (top_k <= kWarpMaxK): free-running consumer warps with private candidate
+//     buffers, a threshold raised from a sorted list of stage maxima; described at WarpSampleOp.
+//   sample_wide_kernel (larger top_k): lockstep stages; each thread marks, in a register bitmask,
+//     the vectors of the stage whose maximum reaches X, moves their passing elements into its own
+//     slots, and the CTA prunes the candidates to the exact top-k (raising X) when more than
+//     k + kPruneSlack are held. The first stage of a segment seeds X: each warp sorts its lanes'
+//     maxima, and the smallest of the warps' ceil(k / warps)-th largest is reached by k elements.
 //
 // The repetition penalty touches only the history ids: at the start of a row segment the distinct
-// ones inside it go into a shared-memory hash set and a list. Each stage inserts the listed ids it
-// holds with their penalised, tempered values; the stream skips set members (looked up only for
-// elements that pass X). So the per-element path carries no penalty work.
-//
-// At the end of a row the exact top-k is ranked into order and the survivor decision runs in double
-// precision on one warp (select_topk.cuh), in exactly the oracle's operation order.
+// ones inside it go into a shared-memory hash set and a list, and the stream skips set members
+// (looked up only for elements that pass X); their penalised values enter separately.
 // Bound: HBM bandwidth (4 bytes per f32 logit, 2 per bf16, read once).
 #include "select_internal.h"
 #include "select_rows.cuh"
