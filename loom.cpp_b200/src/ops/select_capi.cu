@@ -50,13 +50,20 @@ int check_workspace(const void* ws, size_t have, size_t need) {
 
 int map_cuda(cudaError_t e) { return e == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA; }
 
-// CTAs for a streamed call: one per SM, fewer when each would get under kStreamMinRange elements.
-int stream_ctas(int64_t total, int sms) {
-    int64_t g = sms;
+// CTAs for a streamed call of `rows` rows of `width`: up to `slots` (the resident CTAs), fewer when
+// each would get under kStreamMinRange elements. With at least as many rows as CTAs the ranges are
+// whole rows (split_point), and the count is chosen so that every CTA gets the same number of rows:
+// the slowest CTA sets the time, so r = ceil(rows / slots) rows each over ceil(rows / r) CTAs.
+int stream_ctas(int64_t rows, int64_t width, int slots) {
+    int64_t g = slots;
     if (g > kStreamMaxCtas) g = kStreamMaxCtas;
-    const int64_t by_size = total / kStreamMinRange;
+    const int64_t by_size = rows * width / kStreamMinRange;
     if (g > by_size) g = by_size;
     if (g < 1) g = 1;
+    if (rows >= g) {
+        const int64_t per = (rows + g - 1) / g;
+        g = (rows + per - 1) / per;
+    }
     return static_cast<int>(g);
 }
 
@@ -149,7 +156,7 @@ int loom_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     const void* base = static_cast<const unsigned char*>(logits) + lo * esz_of(dtype);
     if (width <= kShortRowMax) return map_cuda(launch_rows_argmax(dtype, base, rows, width, row_stride, lo, out_ids, sms, st));
     const WsLayout l = ws_layout(8, kStreamRecordSlots);
-    const int ctas = stream_ctas(rows * width, sms);
+    const int ctas = stream_ctas(rows, width, sms);
     return map_cuda(launch_argmax_stream(dtype, base, rows, width, row_stride, lo, out_ids, workspace, l, ctas, st));
 }
 
@@ -188,7 +195,7 @@ int loom_sample_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     a.out_topk = out_topk_ids;
     a.shard_out = nullptr;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * n_vocab, kSampleCtasPerSm * sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows, n_vocab, kSampleCtasPerSm * sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 
@@ -223,7 +230,7 @@ int loom_sample_shard_partial(const void* logits, int dtype, int64_t rows, int64
     a.top_k = params->top_k;
     a.shard_out = out_records;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows * shard_vocab, kSampleCtasPerSm * sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows, shard_vocab, kSampleCtasPerSm * sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 

@@ -31,9 +31,12 @@ struct StreamGeom {
     int32_t ctas;       // number of persistent CTAs (ranges)
 };
 
-// Start of range c (its end is split_point(c + 1)).
+// Start of range c (its end is split_point(c + 1)). With at least as many rows as ranges, ranges are
+// whole rows (range c: rows [c * rows / ctas, (c + 1) * rows / ctas)), so no row is split and no
+// partial results are merged; otherwise the flat index space is cut into equal pieces.
 __host__ __device__ __forceinline__ int64_t split_point(const StreamGeom& g, int64_t c) {
     if (c >= g.ctas) return g.total;
+    if (g.rows >= g.ctas) return (c * g.rows / g.ctas) * g.width;
     const int64_t p = c * g.total / g.ctas;
     return p - p % kSplitAlign;
 }
