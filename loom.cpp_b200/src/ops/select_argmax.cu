@@ -54,15 +54,14 @@ struct ArgmaxOp {
         const int32_t nsteps = (nvec + kU * kNT - 1) / (kU * kNT);
         for (int32_t step = 0; step < nsteps; ++step) {
             const int32_t v0 = step * kU * kNT + static_cast<int32_t>(threadIdx.x);
-            Vec16<kDtype> e[kU];
+            uint4 raw[kU];
             float mu = __int_as_float(0x7fc00000); // NaN: fmaxf skips it
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 const int32_t v = v0 + u * kNT;
                 if (v < nvec) {
-                    e[u].unpack(v4[v]);
-#pragma unroll
-                    for (int q = 0; q < kPer; ++q) mu = fmaxf(mu, e[u].x[q]);
+                    raw[u] = v4[v];
+                    mu = fmaxf(mu, vec_max<kDtype>(raw[u]));
                 }
             }
             const bool take = mu > best.v || (mu == best.v && best.i == 0x7fffffff);
@@ -74,8 +73,10 @@ struct ArgmaxOp {
                         const int32_t v = v0 + u * kNT;
                         if (v < nvec) {
                             const int32_t col = static_cast<int32_t>(col0) + v * kPer;
+                            Vec16<kDtype> e;
+                            e.unpack(raw[u]);
 #pragma unroll
-                            for (int q = 0; q < kPer; ++q) arg_offer(b, e[u].x[q], col + q);
+                            for (int q = 0; q < kPer; ++q) arg_offer(b, e.x[q], col + q);
                         }
                     }
                 }

@@ -99,6 +99,23 @@ struct Vec16 {
     }
 };
 
+// Maximum of one 16-byte vector of logits as a float (NaN elements ignored; NaN only if all are
+// NaN; -0 and +0 compare equal). bf16 vectors take the maximum of packed pairs (exact in bf16).
+template <int kDtype>
+__device__ __forceinline__ float vec_max(uint4 raw) {
+    if constexpr (kDtype == LOOM_SELECT_BF16) {
+        const __nv_bfloat162 a = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        const __nv_bfloat162 b = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&raw.z),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&raw.w));
+        const __nv_bfloat162 c = __hmax2(a, b);
+        return fmaxf(__low2float(c), __high2float(c));
+    } else {
+        return fmaxf(fmaxf(__uint_as_float(raw.x), __uint_as_float(raw.y)),
+                     fmaxf(__uint_as_float(raw.z), __uint_as_float(raw.w)));
+    }
+}
+
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"

@@ -739,19 +739,6 @@ __device__ int warp_keep_best(uint64_t* w, int n, int k) {
     return warp_keep_best_p<8>(w, n, k);
 }
 
-// Maximum of one 16-byte vector of logits (NaN elements ignored; NaN only if all are NaN).
-template <int kDtype>
-__device__ __forceinline__ float vec_max(uint4 raw) {
-    Vec16<kDtype> e;
-    e.unpack(raw);
-    if constexpr (kDtype == LOOM_SELECT_BF16) {
-        return fmaxf(fmaxf(fmaxf(e.x[0], e.x[1]), fmaxf(e.x[2], e.x[3])),
-                     fmaxf(fmaxf(e.x[4], e.x[5]), fmaxf(e.x[6], e.x[7])));
-    } else {
-        return fmaxf(fmaxf(e.x[0], e.x[1]), fmaxf(e.x[2], e.x[3]));
-    }
-}
-
 template <int kDtype>
 struct WarpSampleOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
