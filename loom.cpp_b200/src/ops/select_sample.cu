@@ -13,7 +13,7 @@
 //   sample_wide_kernel (larger top_k): lockstep stages; each thread marks, in a register bitmask,
 //     the vectors of the stage whose maximum reaches X, moves their passing elements into its own
 //     slots, and the CTA prunes the candidates to the exact top-k (raising X) when more than
-//     k + kPruneSlack are held. The first stage of a segment seeds X: each warp sorts its lanes'
+//     k + max(kPruneSlack, k) are held. The first stage of a segment seeds X: each warp sorts its lanes'
 //     maxima, and the smallest of the warps' ceil(k / warps)-th largest is reached by k elements.
 //
 // The repetition penalty touches only the history ids: at the start of a row segment the distinct
@@ -36,7 +36,7 @@ constexpr int kSampStages = 2;
 constexpr int kSampStageBytes = 32768;
 constexpr int kSlots = 4;           // raw candidates a thread holds between prunes
 constexpr int kCandCap = 2176;      // candidate rank keys in shared memory
-constexpr int kPruneSlack = 64;     // prune at a stage end when more than k + this many are held
+constexpr int kPruneSlack = 64;     // prune at a stage end when more than k + max(this, k) are held
 constexpr int kHashSlots = 2048;    // history hash set (load <= 1/2 at kMaxHistory ids)
 constexpr int kDecideSlots = 1024;
 constexpr uint32_t kPenalisedFlag = 0x80000000u;  // a raw slot holding a history id's raw value
@@ -585,7 +585,8 @@ struct WideSampleOp {
             const bool failed = sh->fail != 0;
             int held = sh->K;
             for (int w = 0; w < kSampWarps; ++w) held += sh->wcnt[w];
-            if (!failed && held <= p.k + kPruneSlack) break;
+            // prune when the held keys exceed k by the slack (at least k: the prune sorts ~k keys)
+            if (!failed && held <= p.k + (p.k > kPruneSlack ? p.k : kPruneSlack)) break;
             group_sync<kNT>();
             prune<kNT>(p, cand, slots, hset, qn, sh);
             if (!failed) break;
