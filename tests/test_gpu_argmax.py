@@ -120,7 +120,7 @@ def test_greedy_decode_512_steps(sel, dev, oracle):
     np.testing.assert_array_equal(out.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("rows", [1, 3, 148, 1024])
+@pytest.mark.parametrize("rows", [1, 3, 148, 149, 300, 1024])
 def test_batch_vs_oracle(sel, dev, oracle, rows):
     x, _, _ = synth.sample_chain(rows, device="cuda")
     np.testing.assert_array_equal(_ids(sel, x), oracle.argmax_rows(x.cpu().numpy(), nthreads=NT))

@@ -85,6 +85,14 @@ def test_split_rows(sel, dev, oracle, rows):
     vs_oracle(sel, oracle, x, hist, u, 0.7, 1.1, 40, 0.9)
 
 
+@pytest.mark.parametrize("rows,k", [(300, 40), (597, 40), (297, 300)])
+def test_whole_row_ranges(sel, dev, oracle, rows, k):
+    # at least as many rows as CTAs: each CTA takes whole rows, the same number each (300 rows on a
+    # B200: 150 CTAs of 2; 597: 199 of 3), for both kernels (k <= 128 and k > 128)
+    x, hist, u = synth.sample_chain(rows, seed=rows + 7, device="cuda")
+    vs_oracle(sel, oracle, x, hist, u, 0.7, 1.1, k, 0.9)
+
+
 @pytest.mark.parametrize("T,r,k,p", [(1.0, 1.0, 1, 1.0), (0.3, 1.5, 1024, 0.95), (2.0, 0.7, 64, 0.5),
                                      (0.0, 1.1, 40, 0.9), (1e-3, 1.0, 7, 0.999), (25.0, 1.05, 200, 1.0)])
 def test_parameters(sel, dev, oracle, T, r, k, p):
