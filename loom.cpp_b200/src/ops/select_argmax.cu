@@ -13,7 +13,7 @@ namespace {
 
 constexpr int kArgWarps = 8;
 constexpr int kArgNT = kArgWarps * 32;
-constexpr int kArgStages = 4;
+constexpr int kArgStages = 3;  // two CTAs per SM, 96 KB of ring each
 constexpr int kArgStageBytes = 32768;
 
 struct ArgRecord {
@@ -136,7 +136,7 @@ struct ArgmaxOp {
 };
 
 template <int kDtype>
-__global__ void __launch_bounds__((kArgWarps + 1) * 32, 1)
+__global__ void __launch_bounds__((kArgWarps + 1) * 32, 2)
     argmax_stream_kernel(StreamGeom g, int64_t lo, int32_t* out_ids, ArgRecord* records, int* tickets, int* status) {
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ StreamCtl ctl;

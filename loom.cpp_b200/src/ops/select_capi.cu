@@ -156,7 +156,7 @@ int loom_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     const void* base = static_cast<const unsigned char*>(logits) + lo * esz_of(dtype);
     if (width <= kShortRowMax) return map_cuda(launch_rows_argmax(dtype, base, rows, width, row_stride, lo, out_ids, sms, st));
     const WsLayout l = ws_layout(8, kStreamRecordSlots);
-    const int ctas = stream_ctas(rows, width, sms);
+    const int ctas = stream_ctas(rows, width, 2 * sms);  // two argmax CTAs per SM
     return map_cuda(launch_argmax_stream(dtype, base, rows, width, row_stride, lo, out_ids, workspace, l, ctas, st));
 }
 
