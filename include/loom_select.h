@@ -26,7 +26,9 @@
  *     return as soon as the work is enqueued. Calls never allocate: scratch memory is the caller's
  *     `workspace`, sized by the matching *_workspace_size query and zeroed once with
  *     loom_select_workspace_init before its first use. Kernels leave it zeroed again on success.
- *     One workspace must not be used by two calls that can run at the same time.
+ *     One workspace must not be used by two calls that can run at the same time. The one exception
+ *     is loom_sample_rows_noalloc, which takes no workspace: it uses a fixed scratch array inside
+ *     the library and clears what it needs of it on every call.
  *   - Every function returns an int status (LOOM_SELECT_OK = 0). Argument errors are found on the
  *     host before anything is enqueued. Errors that only the device can see (a history id outside
  *     the vocabulary, a bounded wait that gave up) are recorded in the workspace and returned by
@@ -158,7 +160,8 @@ LOOM_SELECT_API int loom_sample_rows(const void* logits, int dtype, int64_t rows
  *   - calls whose work can overlap on the GPU (other streams, other host threads) race on the array:
  *     order them on one stream;
  *   - the first call on a device looks the array up and loads its code there; make it before any
- *     stream capture;
+ *     stream capture; the address is kept until the process exits, so do not use this entry point
+ *     on a device after cudaDeviceReset there;
  *   - out_status (device int32, may be NULL) receives the call's device-side status
  *     (LOOM_SELECT_EHISTORY, LOOM_SELECT_ETIMEOUT or 0), the word loom_select_read_status reads for
  *     a caller-owned workspace.

@@ -14,7 +14,8 @@
 //
 // Errors throw loom::Error -- the engine's own class when include/loom/loom_errors.h is on the
 // include path, otherwise a class of the same name and base declared here.
-// Unlike the C-ABI, these helpers allocate: each thread keeps one growing device workspace.
+// Unlike the C-ABI, these helpers allocate, but only to grow: each thread keeps one device workspace,
+// one device output area and one pinned host area, reused by every later call that fits in them.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -50,60 +51,93 @@ inline void check_cuda(cudaError_t e, const std::string& what) {
     if (e != cudaSuccess) throw Error(what + ": " + cudaGetErrorString(e));
 }
 
-// A per-thread device workspace, zeroed when (re)allocated.
-class Workspace {
+// Per-thread state of the helpers below: one device workspace (zeroed when it is (re)allocated),
+// one device area for a call's outputs and one pinned host area to read them back into. Each grows
+// only when a call needs more than it holds, so after the first call of a given size the helpers
+// allocate no memory on the device or in pinned host memory. The areas belong to the device that
+// was current when they were made; a call on another device makes new ones.
+class ThreadState {
 public:
-    ~Workspace() {
-        if (ptr_) cudaFree(ptr_);
-    }
-    void* get(size_t bytes, cudaStream_t stream) {
-        int dev = -1;
-        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-        if (!ptr_ || bytes > size_ || dev != dev_) {
-            if (ptr_) cudaFree(ptr_);
-            ptr_ = nullptr;
-            check_cuda(cudaMalloc(&ptr_, bytes), "cudaMalloc(workspace)");
-            size_ = bytes;
-            dev_ = dev;
-            check(loom_select_workspace_init(ptr_, size_, stream), "loom_select_workspace_init");
+    ~ThreadState() { release(); }
+    void* workspace(size_t bytes, cudaStream_t stream) {
+        on_current_device();
+        if (bytes > ws_size_) {
+            if (ws_) cudaFree(ws_);
+            ws_ = nullptr;
+            ws_size_ = 0;
+            check_cuda(cudaMalloc(&ws_, bytes), "cudaMalloc(workspace)");
+            ws_size_ = bytes;
+            check(loom_select_workspace_init(ws_, ws_size_, stream), "loom_select_workspace_init");
         }
-        return ptr_;
+        return ws_;
     }
-    size_t size() const { return size_; }
+    size_t workspace_size() const { return ws_size_; }
+    // Device memory for `bytes` of outputs (256-byte aligned).
+    void* device_out(size_t bytes) {
+        on_current_device();
+        if (bytes > dout_size_) {
+            if (dout_) cudaFree(dout_);
+            dout_ = nullptr;
+            dout_size_ = 0;
+            check_cuda(cudaMalloc(&dout_, bytes), "cudaMalloc(outputs)");
+            dout_size_ = bytes;
+        }
+        return dout_;
+    }
+    // Pinned host memory for `bytes` read back from device_out.
+    void* host_out(size_t bytes) {
+        if (bytes > hout_size_) {
+            if (hout_) cudaFreeHost(hout_);
+            hout_ = nullptr;
+            hout_size_ = 0;
+            check_cuda(cudaMallocHost(&hout_, bytes), "cudaMallocHost(outputs)");
+            hout_size_ = bytes;
+        }
+        return hout_;
+    }
 
 private:
-    void* ptr_ = nullptr;
-    size_t size_ = 0;
+    void on_current_device() {
+        int dev = -1;
+        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+        if (dev != dev_) {
+            release_device();
+            dev_ = dev;
+        }
+    }
+    void release_device() {
+        if (ws_) cudaFree(ws_);
+        if (dout_) cudaFree(dout_);
+        ws_ = dout_ = nullptr;
+        ws_size_ = dout_size_ = 0;
+    }
+    void release() {
+        release_device();
+        if (hout_) cudaFreeHost(hout_);
+        hout_ = nullptr;
+        hout_size_ = 0;
+    }
+    void* ws_ = nullptr;
+    size_t ws_size_ = 0;
+    void* dout_ = nullptr;
+    size_t dout_size_ = 0;
+    void* hout_ = nullptr;
+    size_t hout_size_ = 0;
     int dev_ = -1;
 };
 
-inline Workspace& workspace() {
-    thread_local Workspace ws;
-    return ws;
+inline ThreadState& state() {
+    thread_local ThreadState st;
+    return st;
 }
 
-template <class T>
-class DeviceBuffer {
-public:
-    explicit DeviceBuffer(size_t n) {
-        if (n) check_cuda(cudaMalloc(&p_, n * sizeof(T)), "cudaMalloc");
-    }
-    ~DeviceBuffer() {
-        if (p_) cudaFree(p_);
-    }
-    DeviceBuffer(const DeviceBuffer&) = delete;
-    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
-    T* get() const { return p_; }
+inline size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
-private:
-    T* p_ = nullptr;
-};
-
-template <class T>
-std::vector<T> to_host(const T* d, size_t n, cudaStream_t stream) {
-    std::vector<T> h(n);
-    if (n) {
-        check_cuda(cudaMemcpyAsync(h.data(), d, n * sizeof(T), cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync");
+// Copies `bytes` of device outputs to the thread's pinned host area and waits for them.
+inline const void* read_back(const void* d, size_t bytes, cudaStream_t stream) {
+    void* h = state().host_out(bytes > 0 ? bytes : 1);
+    if (bytes) {
+        check_cuda(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync");
         check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     }
     return h;
@@ -126,12 +160,13 @@ inline int64_t argmax_tensor_row(const float* d_logits, int64_t n_vocab, int64_t
         throw Error(std::string(fname) + ": id window [" + std::to_string(lo) + ", " + std::to_string(hi) +
                     ") is not a non-empty sub-range of this output's " + std::to_string(n_vocab) + " class(es)");
     }
-    detail::DeviceBuffer<int32_t> out(1);
-    void* ws = detail::workspace().get(loom_argmax_workspace_size(1, n_vocab), stream);
-    detail::check(loom_argmax_rows(d_logits + row * row_stride, LOOM_SELECT_F32, 1, n_vocab, n_vocab, lo, hi, out.get(),
-                                   ws, detail::workspace().size(), stream),
+    detail::ThreadState& st = detail::state();
+    void* ws = st.workspace(loom_argmax_workspace_size(1, n_vocab), stream);
+    int32_t* out = static_cast<int32_t*>(st.device_out(sizeof(int32_t)));
+    detail::check(loom_argmax_rows(d_logits + row * row_stride, LOOM_SELECT_F32, 1, n_vocab, n_vocab, lo, hi, out, ws,
+                                   st.workspace_size(), stream),
                   fname);
-    return detail::to_host(out.get(), 1, stream)[0];
+    return *static_cast<const int32_t*>(detail::read_back(out, sizeof(int32_t), stream));
 }
 
 // argmax_tensor_rows (src/core/lua_bridge.cpp:343-365): one id per row, in row order, as the Lua
@@ -142,13 +177,15 @@ inline std::vector<double> argmax_tensor_rows(const float* d_logits, int64_t n_c
         throw Error(std::string(fname) + ": output is " + std::to_string(n_classes) + "x" + std::to_string(n_rows) +
                     ", which has no rows to reduce");
     }
-    detail::DeviceBuffer<int32_t> out(static_cast<size_t>(n_rows));
-    void* ws = detail::workspace().get(loom_argmax_workspace_size(n_rows, n_classes), stream);
-    detail::check(loom_argmax_rows(d_logits, LOOM_SELECT_F32, n_rows, n_classes, row_stride, 0, -1, out.get(), ws,
-                                   detail::workspace().size(), stream),
+    detail::ThreadState& st = detail::state();
+    const size_t bytes = static_cast<size_t>(n_rows) * sizeof(int32_t);
+    void* ws = st.workspace(loom_argmax_workspace_size(n_rows, n_classes), stream);
+    int32_t* out = static_cast<int32_t*>(st.device_out(bytes));
+    detail::check(loom_argmax_rows(d_logits, LOOM_SELECT_F32, n_rows, n_classes, row_stride, 0, -1, out, ws,
+                                   st.workspace_size(), stream),
                   fname);
-    const std::vector<int32_t> ids = detail::to_host(out.get(), static_cast<size_t>(n_rows), stream);
-    return std::vector<double>(ids.begin(), ids.end());
+    const int32_t* ids = static_cast<const int32_t*>(detail::read_back(out, bytes, stream));
+    return std::vector<double>(ids, ids + n_rows);
 }
 
 // Generator::argmax (src/core/generation.cpp:64-74) on one device row of n_vocab floats.
@@ -160,13 +197,21 @@ inline int32_t argmax(const float* d_row, int64_t n_vocab, cudaStream_t stream =
 inline std::vector<int32_t> ctc_greedy_decode(const float* d_logits, int64_t n_frames, int64_t n_classes,
                                               int32_t blank_id, cudaStream_t stream = nullptr) {
     if (n_frames <= 0) return {};
-    detail::DeviceBuffer<int32_t> ids(static_cast<size_t>(n_frames)), frames(static_cast<size_t>(n_frames)), len(1);
-    void* ws = detail::workspace().get(loom_ctc_workspace_size(1, n_frames), stream);
-    detail::check(loom_ctc_greedy(d_logits, LOOM_SELECT_F32, 1, n_frames, n_classes, blank_id, ids.get(), frames.get(),
-                                  len.get(), nullptr, nullptr, ws, detail::workspace().size(), stream),
+    // device outputs: [len (256 B)] [ids: n_frames] [frames: n_frames]; len and ids come back in one copy
+    detail::ThreadState& st = detail::state();
+    const size_t ids_bytes = detail::align256(static_cast<size_t>(n_frames) * sizeof(int32_t));
+    void* ws = st.workspace(loom_ctc_workspace_size(1, n_frames), stream);
+    unsigned char* d = static_cast<unsigned char*>(st.device_out(256 + 2 * ids_bytes));
+    int32_t* len = reinterpret_cast<int32_t*>(d);
+    int32_t* ids = reinterpret_cast<int32_t*>(d + 256);
+    int32_t* frames = reinterpret_cast<int32_t*>(d + 256 + ids_bytes);
+    detail::check(loom_ctc_greedy(d_logits, LOOM_SELECT_F32, 1, n_frames, n_classes, blank_id, ids, frames, len, nullptr,
+                                  nullptr, ws, st.workspace_size(), stream),
                   "ctc_greedy_decode");
-    const int32_t n = detail::to_host(len.get(), 1, stream)[0];
-    return detail::to_host(ids.get(), static_cast<size_t>(n), stream);
+    const unsigned char* h = static_cast<const unsigned char*>(detail::read_back(d, 256 + ids_bytes, stream));
+    const int32_t n = *reinterpret_cast<const int32_t*>(h);
+    const int32_t* hid = reinterpret_cast<const int32_t*>(h + 256);
+    return std::vector<int32_t>(hid, hid + n);
 }
 
 struct SampleResult {
@@ -179,18 +224,22 @@ struct SampleResult {
 inline SampleResult sample_rows(const float* d_logits, int64_t rows, int64_t n_vocab, int64_t row_stride,
                                 const int32_t* d_history, int32_t history_len, const float* d_u,
                                 const loom_sample_params& params, cudaStream_t stream = nullptr) {
-    detail::DeviceBuffer<int32_t> ids(static_cast<size_t>(rows > 0 ? rows : 0));
-    detail::DeviceBuffer<float> probs(static_cast<size_t>(rows > 0 ? rows : 0));
-    void* ws = detail::workspace().get(loom_sample_workspace_size(rows, n_vocab, params.top_k), stream);
+    const size_t n = static_cast<size_t>(rows > 0 ? rows : 0);
+    const size_t ids_bytes = detail::align256(n * sizeof(int32_t));
+    detail::ThreadState& st = detail::state();
+    void* ws = st.workspace(loom_sample_workspace_size(rows, n_vocab, params.top_k), stream);
+    unsigned char* d = static_cast<unsigned char*>(st.device_out(ids_bytes + n * sizeof(float) + 1));
+    int32_t* ids = reinterpret_cast<int32_t*>(d);
+    float* probs = reinterpret_cast<float*>(d + ids_bytes);
     detail::check(loom_sample_rows(d_logits, LOOM_SELECT_F32, rows, n_vocab, row_stride, d_history, history_len, d_u,
-                                   &params, ids.get(), probs.get(), nullptr, nullptr, ws, detail::workspace().size(),
-                                   stream),
+                                   &params, ids, probs, nullptr, nullptr, ws, st.workspace_size(), stream),
                   "sample_rows");
-    const int st = loom_select_read_status(ws, stream);
-    if (st != LOOM_SELECT_OK) detail::check(st, "sample_rows");
+    const int status = loom_select_read_status(ws, stream);
+    if (status != LOOM_SELECT_OK) detail::check(status, "sample_rows");
+    const unsigned char* h = static_cast<const unsigned char*>(detail::read_back(d, ids_bytes + n * sizeof(float), stream));
     SampleResult r;
-    r.ids = detail::to_host(ids.get(), static_cast<size_t>(rows), stream);
-    r.probs = detail::to_host(probs.get(), static_cast<size_t>(rows), stream);
+    r.ids.assign(reinterpret_cast<const int32_t*>(h), reinterpret_cast<const int32_t*>(h) + n);
+    r.probs.assign(reinterpret_cast<const float*>(h + ids_bytes), reinterpret_cast<const float*>(h + ids_bytes) + n);
     return r;
 }
 

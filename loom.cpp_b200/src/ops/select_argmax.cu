@@ -3,6 +3,8 @@
 // Replaces the host scan of Generator::argmax (src/core/generation.cpp:64-74) and argmax_tensor_row /
 // argmax_tensor_rows (src/core/lua_bridge.cpp:320-329, :358-362) for rows too long for one warp.
 // Bound: HBM bandwidth (4 or 2 bytes read per element, one compare per element).
+#include <atomic>
+
 #include "select_internal.h"
 #include "select_rows.cuh"
 #include "select_stream.cuh"
@@ -149,7 +151,7 @@ template <int kDtype>
 cudaError_t launch_argmax_stream_t(const StreamGeom& g, int64_t lo, int32_t* out_ids, ArgRecord* records,
                                    int* tickets, int* status, cudaStream_t stream) {
     constexpr size_t smem = static_cast<size_t>(kArgStages) * kArgStageBytes;
-    static bool configured[64] = {};
+    static std::atomic<bool> configured[64] = {};  // set once per device, from any host thread
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {

@@ -4,6 +4,7 @@
 // src/core/lua_bridge.cpp:302-319 and :350-353 where loom.cpp has them), workspace layout, the choice
 // of kernel and grid, and CUDA error mapping. No allocation, no synchronisation except in
 // loom_select_read_status.
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -14,19 +15,22 @@
 namespace loom_select {
 
 int device_sm_count(int* status) {
-    static int cache[64] = {};
+    static std::atomic<int> cache[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         *status = LOOM_SELECT_ECUDA;
         return 0;
     }
-    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    if (dev >= 0 && dev < 64) {
+        const int c = cache[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
         *status = LOOM_SELECT_ECUDA;
         return 0;
     }
-    if (dev >= 0 && dev < 64) cache[dev] = sms;
+    if (dev >= 0 && dev < 64) cache[dev].store(sms, std::memory_order_relaxed);
     return sms;
 }
 
@@ -49,23 +53,6 @@ int check_workspace(const void* ws, size_t have, size_t need) {
 }
 
 int map_cuda(cudaError_t e) { return e == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA; }
-
-// CTAs for a streamed call of `rows` rows of `width`: up to `slots` (the resident CTAs), fewer when
-// each would get under kStreamMinRange elements. With at least as many rows as CTAs the ranges are
-// whole rows (split_point), and the count is chosen so that every CTA gets the same number of rows:
-// the slowest CTA sets the time, so r = ceil(rows / slots) rows each over ceil(rows / r) CTAs.
-int stream_ctas(int64_t rows, int64_t width, int slots) {
-    int64_t g = slots;
-    if (g > kStreamMaxCtas) g = kStreamMaxCtas;
-    const int64_t by_size = rows * width / kStreamMinRange;
-    if (g > by_size) g = by_size;
-    if (g < 1) g = 1;
-    if (rows >= g) {
-        const int64_t per = (rows + g - 1) / g;
-        g = (rows + per - 1) / per;
-    }
-    return static_cast<int>(g);
-}
 
 int check_params(const loom_sample_params* p, int64_t vocab, bool allow_greedy) {
     if (!p) return LOOM_SELECT_EINVAL;

@@ -45,7 +45,25 @@ inline WsLayout ws_layout(size_t record_bytes, int64_t n_records) {
     return l;
 }
 
-// Number of SMs of the current device (cached per device).
+// CTAs for a streamed call of `rows` rows of `width`: up to `slots` (the resident CTAs), fewer when
+// each would get under kStreamMinRange elements. With at least as many rows as CTAs the ranges are
+// whole rows (split_point), and the count is chosen so that every CTA gets the same number of rows:
+// the slowest CTA sets the time, so r = ceil(rows / slots) rows each over ceil(rows / r) CTAs.
+inline int stream_ctas(int64_t rows, int64_t width, int slots) {
+    int64_t g = slots;
+    if (g > kStreamMaxCtas) g = kStreamMaxCtas;
+    const int64_t by_size = rows * width / kStreamMinRange;
+    if (g > by_size) g = by_size;
+    if (g < 1) g = 1;
+    if (rows >= g) {
+        const int64_t per = (rows + g - 1) / g;
+        g = (rows + per - 1) / per;
+    }
+    return static_cast<int>(g);
+}
+
+// Number of SMs of the current device (cached per device; the cache is safe to fill from several
+// host threads at once).
 int device_sm_count(int* status);
 
 // Launchers (validated arguments; return a cudaError_t from the launch).

@@ -14,7 +14,9 @@
 // or different host threads) race on it.
 //
 // The first call on a device looks the array's address up (cudaGetSymbolAddress, which also loads this
-// file's device code on that device); make that first call before any stream capture.
+// file's device code on that device); make that first call before any stream capture. The address is
+// kept for the life of the process, so this entry point must not be used on a device after a
+// cudaDeviceReset there (the array may come back at another address).
 #include <cmath>
 #include <mutex>
 
@@ -112,12 +114,9 @@ extern "C" int loom_sample_rows_noalloc(const void* logits, int dtype, int64_t r
     a.shard_out = nullptr;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
     if (l.bytes > kNoAllocScratchBytes) return LOOM_SELECT_ESHAPE;
-    int64_t ctas = static_cast<int64_t>(kSampleCtasPerSm) * sms;
-    if (ctas > kStreamMaxCtas) ctas = kStreamMaxCtas;
-    const int64_t by_size = rows * n_vocab / kStreamMinRange;
-    if (ctas > by_size) ctas = by_size;
-    if (ctas < 1) ctas = 1;
-    if (launch_sample_stream(a, scratch, l, static_cast<int>(ctas), st) != cudaSuccess) return LOOM_SELECT_ECUDA;
+    // the grid loom_sample_rows would launch for the same call
+    const int ctas = stream_ctas(rows, n_vocab, kSampleCtasPerSm * sms);
+    if (launch_sample_stream(a, scratch, l, ctas, st) != cudaSuccess) return LOOM_SELECT_ECUDA;
     // the device-side status word (history ids out of range, a timed-out wait) for the caller
     if (out_status && cudaMemcpyAsync(out_status, scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return LOOM_SELECT_ECUDA;

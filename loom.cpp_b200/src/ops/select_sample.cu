@@ -20,6 +20,8 @@
 // ones inside it go into a shared-memory hash set and a list, and the stream skips set members
 // (looked up only for elements that pass X); their penalised values enter separately.
 // Bound: HBM bandwidth (4 bytes per f32 logit, 2 per bf16, read once).
+#include <atomic>
+
 #include "select_internal.h"
 #include "select_rows.cuh"
 #include "select_stream.cuh"
@@ -1205,7 +1207,7 @@ __global__ void __launch_bounds__(kMergeNT) shard_merge_kernel(const unsigned ch
 
 template <int kDtype>
 cudaError_t launch_sample_t(const StreamGeom& g, const SampleDev& p, cudaStream_t stream) {
-    static bool configured[64] = {};
+    static std::atomic<bool> configured[64] = {};  // set once per device, from any host thread
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -1270,7 +1272,7 @@ cudaError_t launch_shard_merge(const void* records, int32_t n_shards, int64_t ro
                                float top_p, int32_t* out_ids, float* out_prob, float* out_logp, int32_t* out_topk,
                                cudaStream_t stream) {
     const size_t smem = kCandCap * sizeof(uint64_t) + kDecideSlots * sizeof(double);
-    static bool configured[64] = {};
+    static std::atomic<bool> configured[64] = {};  // set once per device, from any host thread
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {

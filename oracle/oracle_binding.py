@@ -14,12 +14,14 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libref_ctc.so")
+REFPATH_PATH = os.path.join(HERE, "librefpath.so")
 
 F32 = 0
 BF16 = 1
 
 _LIB = None
 _REF = None
+_REFPATH = None
 
 
 def build(ref=False):
@@ -81,6 +83,24 @@ def ref_lib():
                                             ctypes.c_void_p, ctypes.c_int64]
         _REF = l
     return _REF
+
+
+def refpath_lib():
+    """librefpath.so: loom.cpp's host path (device-to-host copy per row, then the scan), timed in C."""
+    global _REFPATH
+    if _REFPATH is None:
+        if not os.path.exists(REFPATH_PATH):
+            subprocess.run(["make", "-s", "-C", HERE, "librefpath.so"], check=True)
+        l = ctypes.CDLL(REFPATH_PATH)
+        vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+        l.refpath_greedy_decode.restype = ctypes.c_double
+        l.refpath_greedy_decode.argtypes = [vp, i64, i64, i64, vp]
+        l.refpath_argmax_tensor_rows.restype = ctypes.c_double
+        l.refpath_argmax_tensor_rows.argtypes = [vp, i64, i64, i64, vp]
+        l.refpath_ctc_driver.restype = ctypes.c_double
+        l.refpath_ctc_driver.argtypes = [vp, i64, i64, i64, i32, vp, vp]
+        _REFPATH = l
+    return _REFPATH
 
 
 def _dtype_of(a):

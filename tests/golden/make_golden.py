@@ -72,7 +72,7 @@ def adversarial_rows(rng, n=37):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("LOOM_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("LOOM_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference"))
     a = ap.parse_args()
     os.environ["REF"] = a.reference
     import subprocess

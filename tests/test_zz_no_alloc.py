@@ -1,8 +1,8 @@
 """loom_sample_rows_noalloc (the sampling chain on the library's own fixed scratch) against loom_sample_rows.
 
 Collected last on purpose: it must give the same results whether it runs alone in a fresh process
-(its first call looks the scratch up on the device) or after every other test. Two calls in a row
-share the scratch, so the second one also checks that the first left it fit for reuse. Ids and top-k
+(its first call looks the scratch up on the device) or after every other test. Calls in a row
+share the scratch, so each one after the first also checks that the one before left it fit for reuse. Ids and top-k
 sets must be equal; probabilities within 1e-5 relative, log-probs within 1e-5 on the probability
 scale (the tolerance of the sampling tests; both entry points run the same kernel).
 """
@@ -49,23 +49,24 @@ def assert_same(got, want):
     assert np.all(np.abs(gl[fin] - wl[fin]) <= LOGP_TOL * np.maximum(1.0, np.abs(wl[fin])))
 
 
-def test_two_calls_in_a_row_match_loom_sample_rows(sel, dev):
-    # call 1: [512, 151936] f32 with a 256-id history (rows cut across CTAs); call 2: [96, 262144] bf16
-    # without history at the largest top-k this entry point takes. Both are enqueued before either is
-    # read back, so the second runs on the scratch the first just used.
+def test_calls_in_a_row_match_loom_sample_rows(sel, dev):
+    # call 1: [512, 151936] f32 with a 256-id history (at least as many rows as CTAs: whole rows per
+    # CTA, no tickets); call 2: [96, 262144] bf16 without history at the largest top-k this entry point
+    # takes (fewer rows than CTAs: rows cut across CTAs, merged through the tickets and records of the
+    # scratch); call 3: [40, 151936] f32 with history, again cut across CTAs, on the tickets call 2
+    # just used. All are enqueued before any is read back, so each runs on the scratch the one before
+    # it left behind.
     x1, h1, u1 = synth.sample_chain(512, seed=41, device="cuda")
     x2, u2 = synth.gemma_vocab(96, seed=43, device="cuda")
-    a = (x1, h1, u1, 0.7, 1.1, 40, 0.9)
-    b = (x2, None, u2, 1.3, 1.0, 64, 0.95)
-    got_a = without_workspace(sel, *a)
-    got_b = without_workspace(sel, *b)
+    x3, h3, u3 = synth.sample_chain(40, seed=47, device="cuda")
+    calls = [(x1, h1, u1, 0.7, 1.1, 40, 0.9), (x2, None, u2, 1.3, 1.0, 64, 0.95), (x3, h3, u3, 0.8, 1.2, 50, 0.8)]
+    got = [without_workspace(sel, *c) for c in calls]
     torch.cuda.synchronize()
-    want_a = with_workspace(sel, *a)
-    want_b = with_workspace(sel, *b)
+    want = [with_workspace(sel, *c) for c in calls]
     torch.cuda.synchronize()
-    assert got_a[4].item() == sel.OK and got_b[4].item() == sel.OK
-    assert_same(got_a, want_a)
-    assert_same(got_b, want_b)
+    for g, w in zip(got, want):
+        assert g[4].item() == sel.OK
+        assert_same(g, w)
 
 
 def test_device_status_and_size_limit(sel, dev):
