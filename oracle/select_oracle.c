@@ -629,3 +629,70 @@ int oracle_shard_merge(const void* records, int32_t n_shards, int64_t rows, cons
     free(heap);
     return status;
 }
+
+/* ---- check of the kernels' division by T (test infrastructure) ----
+ * The log-sum-exp of the sampling kernels divides each logit by T without a divide instruction, by
+ * Markstein's method: with inv = fl(1 / T), q0 = fl(x * inv), r = x - T * q0 (exact, one FMA) and
+ * q = fl(q0 + r * inv) (one FMA). This counts, for every float mantissa of x in [1, 2) and each given
+ * T, the x where q differs from the IEEE quotient x / T. The rounding of x / T depends on the
+ * mantissas only (away from overflow and subnormals), so [1, 2) covers every x. */
+static float div_markstein(float x, float T, float inv) {
+    const float q0 = x * inv;
+    const float r = fmaf(-q0, T, x);
+    return fmaf(r, inv, q0);
+}
+
+typedef struct {
+    const float* T;
+    int64_t nT, t0, t1;
+    int64_t bad;
+    float bad_x, bad_T;
+} div_job;
+
+static void* div_worker(void* arg) {
+    div_job* j = (div_job*)arg;
+    for (int64_t t = j->t0; t < j->t1; ++t) {
+        const float T = j->T[t];
+        const float inv = 1.0f / T;
+        for (uint32_t m = 0; m < (1u << 23); ++m) {
+            uint32_t bits = 0x3f800000u | m;
+            float x;
+            memcpy(&x, &bits, sizeof x);
+            const float want = x / T;
+            const float got = div_markstein(x, T, inv);
+            if (memcmp(&want, &got, sizeof want) != 0) {
+                if (j->bad == 0) {
+                    j->bad_x = x;
+                    j->bad_T = T;
+                }
+                ++j->bad;
+            }
+        }
+    }
+    return NULL;
+}
+
+int64_t oracle_div_check(const float* T, int64_t nT, int nthreads, float* bad_x, float* bad_T) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 64) nthreads = 64;
+    pthread_t th[64];
+    div_job jobs[64];
+    for (int i = 0; i < nthreads; ++i) {
+        jobs[i].T = T;
+        jobs[i].nT = nT;
+        jobs[i].t0 = nT * i / nthreads;
+        jobs[i].t1 = nT * (i + 1) / nthreads;
+        jobs[i].bad = 0;
+        pthread_create(&th[i], NULL, div_worker, &jobs[i]);
+    }
+    int64_t bad = 0;
+    for (int i = 0; i < nthreads; ++i) {
+        pthread_join(th[i], NULL);
+        if (jobs[i].bad && !bad) {
+            *bad_x = jobs[i].bad_x;
+            *bad_T = jobs[i].bad_T;
+        }
+        bad += jobs[i].bad;
+    }
+    return bad;
+}

@@ -78,6 +78,10 @@ int oracle_shard_merge(const void* records, int32_t n_shards, int64_t rows, cons
 /* loom_exp_d of include/loom_select_math.h, exported so the tests can measure it against libm. */
 double oracle_exp_d(double x);
 
+/* Test helper: mismatches of the kernels' division by T (Markstein's method) against x / T, over every
+ * x mantissa in [1, 2) and the nT given T values (see select_oracle.c). */
+int64_t oracle_div_check(const float* T, int64_t nT, int nthreads, float* bad_x, float* bad_T);
+
 #ifdef __cplusplus
 }
 #endif

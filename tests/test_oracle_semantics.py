@@ -6,6 +6,7 @@ distinct history ids, fp32 temperature divide, key = value desc / id asc with Na
 a second time with numpy sorting and Python floats, and checks the C oracle against it.
 """
 import math
+import os
 
 import numpy as np
 import pytest
@@ -160,3 +161,24 @@ def test_exp_d_accuracy(oracle):
     assert oracle.exp_d(0.0) == 1.0
     assert oracle.exp_d(-800.0) == 0.0
     assert math.isnan(oracle.exp_d(float("nan")))
+
+
+def test_kernel_division_by_temperature_equals_ieee_divide(oracle):
+    """The sampling kernels divide by T (and by the penalty r) with Markstein's method -- a product with
+    the correctly rounded reciprocal and one FMA correction -- instead of a divide instruction. That
+    must give the IEEE quotient bit for bit: checked for every float mantissa of x against 64
+    divisors (the headline's T 0.7 and r 1.1, extremes, and seeded random ones)."""
+    import ctypes
+
+    import numpy as np
+
+    f = oracle.lib().oracle_div_check
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    rng = np.random.default_rng(20261202)
+    fixed = [0.7, 0.001, 1.3, 2.5, 0.9, 1.0, 0.5, 0.25, 3.0, 1e-4, 1e4, 0.1, 0.3333333, 1.9999999, 1.0000001,
+             0.99999994, 1.1, 1.2, 1.05, 0.8, 1.5, 2.0]
+    Ts = np.concatenate([np.array(fixed, np.float32), (2.0 ** rng.uniform(-12, 12, 42)).astype(np.float32)])
+    bx, bT = ctypes.c_float(), ctypes.c_float()
+    bad = f(Ts.ctypes.data, len(Ts), os.cpu_count() or 1, ctypes.byref(bx), ctypes.byref(bT))
+    assert bad == 0, f"{bad} mismatches, first at x={bx.value!r}, T={bT.value!r}"
