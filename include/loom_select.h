@@ -113,6 +113,28 @@ LOOM_SELECT_API int loom_argmax_rows(const void* logits, int dtype, int64_t rows
                      int64_t lo, int64_t hi, int32_t* out_ids, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Largest number of id windows one loom_argmax_windows call takes. */
+#define LOOM_SELECT_MAX_WINDOWS 8
+
+/* Workspace size in bytes for loom_argmax_windows on `rows` rows and `n_windows` windows. */
+LOOM_SELECT_API size_t loom_argmax_windows_workspace_size(int64_t rows, int32_t n_windows);
+
+/*
+ * Greedy argmax of every row over each of several id windows, in one launch:
+ * out_ids[r * n_windows + w] = the ABSOLUTE argmax id of row r over [lo[w], hi[w]), by the
+ * loom_argmax_rows rule (strict '>' from lo[w]; a NaN at lo[w] wins; -0 == +0).
+ *
+ * Replaces n_windows calls per row of argmax_tensor_row (src/core/lua_bridge.cpp:302-330), the scan
+ * behind loom.argmax_row_range (lua_bridge.cpp:779-797): Whisper's driver asks one decoder row for its
+ * language block and its timestamp block, each a window inside the 51865-id vocabulary.
+ * lo and hi are HOST arrays of n_windows (1 .. LOOM_SELECT_MAX_WINDOWS) entries, read during the call;
+ * hi[w] < 0 means n_vocab. Errors, before anything is enqueued: LOOM_SELECT_EWINDOW for a window with
+ * lo < 0, lo >= hi or hi > n_vocab (lua_bridge.cpp:315-319); LOOM_SELECT_EINVAL for n_windows out of range.
+ */
+LOOM_SELECT_API int loom_argmax_windows(const void* logits, int dtype, int64_t rows, int64_t n_vocab,
+                                        int64_t row_stride, const int64_t* lo, const int64_t* hi, int32_t n_windows,
+                                        int32_t* out_ids, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Sampling parameters (passed by pointer to host memory; read during the call). */
 typedef struct loom_sample_params {
     float temperature;        /* T > 0, finite; T == 0 selects greedy (loom_argmax_rows semantics) */
@@ -167,7 +189,7 @@ LOOM_SELECT_API int loom_sample_rows(const void* logits, int dtype, int64_t rows
  *     a caller-owned workspace.
  */
 #define LOOM_SELECT_NOALLOC_MAX_TOP_K 64
-#define LOOM_SELECT_NOALLOC_SCRATCH_BYTES 1089792 /* 256 + 8192 + 2048 * (16 + 8 * 64) */
+#define LOOM_SELECT_NOALLOC_SCRATCH_BYTES 1106176 /* 256 + 8192 + 16384 + 2048 * (16 + 8 * 64) */
 
 LOOM_SELECT_API int loom_sample_rows_noalloc(const void* logits, int dtype, int64_t rows, int64_t n_vocab,
                              int64_t row_stride, const int32_t* history, int32_t history_len, const float* u,

@@ -19,7 +19,13 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libloom_select.so")
 OBJDIR = os.path.join(ROOT, "_build", "loom_select")
 
-SOURCES = ["select_capi.cu", "select_argmax.cu", "select_ctc.cu", "select_sample.cu", "select_noalloc.cu"]
+# (source, object name, extra flags), compiled in parallel
+SOURCES = [("select_capi.cu", "select_capi.o", []),
+           ("select_argmax.cu", "select_argmax.o", []),
+           ("select_ctc.cu", "select_ctc.o", []),
+           ("select_sample.cu", "select_sample.o", []),
+           ("select_noalloc.cu", "select_noalloc.o", []),
+           ("select_windows.cu", "select_windows.o", [])]
 
 # sm_100a only. --fmad=false: no multiply-add contraction anywhere, so every float expression
 # rounds as written (the decision arithmetic also spells its operations as explicit intrinsics).
@@ -54,23 +60,23 @@ def _stale(obj, src, newest_header):
     return os.path.getmtime(src) > t or newest_header > t
 
 
-def build(force=False, jobs=4, verbose=False):
+def build(force=False, jobs=None, verbose=False):
     """Compiles every kernel source for sm_100a and links libloom_select.so. Returns its path."""
     os.makedirs(OBJDIR, exist_ok=True)
     nvcc = _nvcc()
     newest_header = max(os.path.getmtime(h) for h in _headers())
     todo = []
     objs = []
-    for s in SOURCES:
+    for s, oname, extra in SOURCES:
         src = os.path.join(OPS, s)
-        obj = os.path.join(OBJDIR, s.replace(".cu", ".o"))
+        obj = os.path.join(OBJDIR, oname)
         objs.append(obj)
         if force or _stale(obj, src, newest_header):
-            todo.append((src, obj))
+            todo.append((src, obj, extra))
 
     def compile_one(job):
-        src, obj = job
-        cmd = [nvcc] + NVCC_FLAGS + ["-c", src, "-o", obj]
+        src, obj, extra = job
+        cmd = [nvcc] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -78,6 +84,7 @@ def build(force=False, jobs=4, verbose=False):
             raise RuntimeError(f"nvcc failed on {src}:\n{r.stdout}\n{r.stderr}")
         return obj
 
+    jobs = jobs or os.cpu_count() or 4
     with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, jobs)) as ex:
         list(ex.map(compile_one, todo))
 

@@ -26,6 +26,7 @@ LIB_PATH = os.path.join(_HERE, "libloom_select.so")
 F32 = 0
 BF16 = 1
 MAX_TOP_K = 1024
+MAX_WINDOWS = 8
 
 OK = 0
 EINVAL = 1
@@ -48,6 +49,8 @@ EXPORTS = (
     "loom_select_workspace_init",
     "loom_select_read_status",
     "loom_argmax_rows",
+    "loom_argmax_windows_workspace_size",
+    "loom_argmax_windows",
     "loom_sample_rows",
     "loom_sample_rows_noalloc",
     "loom_shard_record_bytes",
@@ -92,6 +95,8 @@ def _lib():
             "loom_select_workspace_init": (ctypes.c_int, [vp, sz, vp]),
             "loom_select_read_status": (ctypes.c_int, [vp, vp]),
             "loom_argmax_rows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
+            "loom_argmax_windows_workspace_size": (sz, [i64, i32]),
+            "loom_argmax_windows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, vp, i32, vp, vp, sz, vp]),
             "loom_sample_rows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, i32, vp,
                                                 ctypes.POINTER(SampleParams), vp, vp, vp, vp, vp, sz, vp]),
             "loom_sample_rows_noalloc": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, i32, vp,
@@ -226,6 +231,29 @@ def argmax_row_range(logits, row, lo, hi, workspace=None, stream=None):
     out = torch.empty(1, dtype=torch.int32, device=logits.device)
     argmax_rows_into(view, out, lo, hi, workspace, stream)
     return float(out.item())
+
+
+def argmax_windows_into(logits, windows, out, workspace=None, stream=None):
+    """Every row's absolute argmax over each [lo, hi) of `windows` (a list of (lo, hi), hi < 0 meaning
+    n_vocab) into the int32 CUDA tensor `out` of shape [rows, len(windows)], in one launch."""
+    rows, n_vocab, stride = _rows_view(logits)
+    n = len(windows)
+    lo = (ctypes.c_int64 * max(n, 1))(*[int(w[0]) for w in windows])
+    hi = (ctypes.c_int64 * max(n, 1))(*[int(w[1]) for w in windows])
+    ws = workspace or default_workspace()
+    buf = ws.get(_lib().loom_argmax_windows_workspace_size(rows, max(n, 1)), stream)
+    check(_lib().loom_argmax_windows(_ptr(logits), _dtype_code(logits), rows, n_vocab, stride, lo, hi, n, _ptr(out),
+                                     _ptr(buf), buf.numel(), _stream_handle(stream)), "loom_argmax_windows")
+    return out
+
+
+def argmax_windows(logits, windows, workspace=None, stream=None):
+    """loom.argmax_row_range over several windows of every row at once: an int32 CUDA tensor
+    [rows, len(windows)] of absolute ids (lua_bridge.cpp:779-797, batched)."""
+    torch = _torch()
+    rows, _, _ = _rows_view(logits)
+    out = torch.empty(rows, len(windows), dtype=torch.int32, device=logits.device)
+    return argmax_windows_into(logits, windows, out, workspace, stream)
 
 
 def argmax_row(logits, row=-1, workspace=None, stream=None):

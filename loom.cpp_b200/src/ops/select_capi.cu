@@ -96,6 +96,35 @@ size_t loom_argmax_workspace_size(int64_t rows, int64_t n_vocab) {
     return ws_layout(8, kStreamRecordSlots).bytes;
 }
 
+size_t loom_argmax_windows_workspace_size(int64_t rows, int32_t n_windows) {
+    if (rows <= 0 || n_windows <= 0) return kWsAlign;
+    return ws_layout(0, 0).bytes;  // the fixed regions: status, tickets, pair records
+}
+
+int loom_argmax_windows(const void* logits, int dtype, int64_t rows, int64_t n_vocab, int64_t row_stride,
+                        const int64_t* lo, const int64_t* hi, int32_t n_windows, int32_t* out_ids, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    if (!dtype_ok(dtype)) return LOOM_SELECT_EDTYPE;
+    if (!logits || !out_ids || !lo || !hi || rows <= 0 || n_vocab <= 0 || row_stride < n_vocab ||
+        n_windows < 1 || n_windows > LOOM_SELECT_MAX_WINDOWS)
+        return LOOM_SELECT_EINVAL;
+    if (n_vocab > INT32_MAX) return LOOM_SELECT_ESHAPE;
+    int64_t wlo[LOOM_SELECT_MAX_WINDOWS], whi[LOOM_SELECT_MAX_WINDOWS];
+    for (int32_t w = 0; w < n_windows; ++w) {
+        wlo[w] = lo[w];
+        whi[w] = hi[w] < 0 ? n_vocab : hi[w];
+        if (wlo[w] < 0 || wlo[w] >= whi[w] || whi[w] > n_vocab) return LOOM_SELECT_EWINDOW;
+    }
+    if (int st = check_workspace(workspace, workspace_bytes, loom_argmax_windows_workspace_size(rows, n_windows)))
+        return st;
+    int status = LOOM_SELECT_OK;
+    const int sms = device_sm_count(&status);
+    if (status) return status;
+    const WsLayout l = ws_layout(0, 0);
+    return map_cuda(launch_argmax_windows(dtype, logits, rows, row_stride, wlo, whi, n_windows, out_ids, workspace, l,
+                                          sms, static_cast<cudaStream_t>(stream)));
+}
+
 size_t loom_sample_workspace_size(int64_t rows, int64_t n_vocab, int32_t top_k) {
     if (rows <= 0 || n_vocab <= 0 || top_k <= 0) return kWsAlign;
     return sample_ws_bytes(rows, top_k);
@@ -142,6 +171,11 @@ int loom_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     const void* base = static_cast<const unsigned char*>(logits) + lo * esz_of(dtype);
     if (width <= kShortRowMax) return map_cuda(launch_rows_argmax(dtype, base, rows, width, row_stride, lo, out_ids, sms, st));
+    if (rows * width <= kChunkArgmaxMaxElems) {
+        // small batches (a decode step): chunks of the rows spread over every SM
+        const WsLayout l = ws_layout(0, 0);
+        return map_cuda(launch_argmax_windows(dtype, logits, rows, row_stride, &lo, &hi, 1, out_ids, workspace, l, sms, st));
+    }
     const WsLayout l = ws_layout(8, kStreamRecordSlots);
     const int ctas = stream_ctas(rows, width, 2 * sms);  // two argmax CTAs per SM
     return map_cuda(launch_argmax_stream(dtype, base, rows, width, row_stride, lo, out_ids, workspace, l, ctas, st));
@@ -182,7 +216,7 @@ int loom_sample_rows(const void* logits, int dtype, int64_t rows, int64_t n_voca
     a.out_topk = out_topk_ids;
     a.shard_out = nullptr;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows, n_vocab, kSampleCtasPerSm * sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, sample_ctas(rows, n_vocab, sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 
@@ -217,7 +251,7 @@ int loom_sample_shard_partial(const void* logits, int dtype, int64_t rows, int64
     a.top_k = params->top_k;
     a.shard_out = out_records;
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
-    return map_cuda(launch_sample_stream(a, workspace, l, stream_ctas(rows, shard_vocab, kSampleCtasPerSm * sms),
+    return map_cuda(launch_sample_stream(a, workspace, l, sample_ctas(rows, shard_vocab, sms),
                                          static_cast<cudaStream_t>(stream)));
 }
 

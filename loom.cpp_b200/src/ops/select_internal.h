@@ -14,6 +14,8 @@ namespace loom_select {
 //   [256, 256 + 8 KiB)    tickets: kTicketSlots int32 at a FIXED place for every call, zero between
 //                         calls (each kernel returns the tickets it used to zero), so calls of any
 //                         size and kind can share one workspace
+//   [.., + 16 KiB)        pair records of the chunked argmax (kChunkPairs x 16 bytes), also zero
+//                         between calls and touched by no other kernel
 //   records / frames      per-call scratch, fully written before it is read
 constexpr size_t kWsAlign = 256;
 inline size_t ws_round(size_t b) { return (b + kWsAlign - 1) / kWsAlign * kWsAlign; }
@@ -31,8 +33,13 @@ constexpr int64_t kTicketSlots = 2 * kStreamMaxCtas;
 // CTC: a CTA holds at most 62 whole utterances and the grid at most kTicketSlots CTAs.
 constexpr int64_t kCtcMaxUtt = kTicketSlots * 62;
 
+// The chunked argmax keeps one 16-byte record per (row, window) pair of a launch, at most this many.
+constexpr int64_t kChunkPairs = 1024;
+constexpr size_t kChunkPairBytes = 16;
+
 struct WsLayout {
     size_t tickets = 0;
+    size_t pairs = 0;
     size_t records = 0;
     size_t bytes = 0;
 };
@@ -40,7 +47,8 @@ struct WsLayout {
 inline WsLayout ws_layout(size_t record_bytes, int64_t n_records) {
     WsLayout l;
     l.tickets = kWsAlign;
-    l.records = l.tickets + ws_round(static_cast<size_t>(kTicketSlots) * sizeof(int32_t));
+    l.pairs = l.tickets + ws_round(static_cast<size_t>(kTicketSlots) * sizeof(int32_t));
+    l.records = l.pairs + ws_round(static_cast<size_t>(kChunkPairs) * kChunkPairBytes);
     l.bytes = l.records + ws_round(record_bytes * static_cast<size_t>(n_records));
     return l;
 }
@@ -71,6 +79,16 @@ cudaError_t launch_argmax_stream(int dtype, const void* window_base, int64_t row
                                  int64_t lo, int32_t* out_ids, void* workspace, const WsLayout& l, int ctas,
                                  cudaStream_t stream);
 
+// Windowed / chunked argmax (select_windows.cu): every (row, window) pair cut into chunks that any CTA
+// takes; a 16-byte record per pair in the workspace's pair region (rows in groups of at most
+// kChunkPairs pairs per launch). loom_argmax_rows sends calls of at most kChunkArgmaxMaxElems
+// elements there.
+constexpr int kArgmaxMaxWindows = LOOM_SELECT_MAX_WINDOWS;
+constexpr int64_t kChunkArgmaxMaxElems = int64_t(16) << 20;
+cudaError_t launch_argmax_windows(int dtype, const void* logits, int64_t rows, int64_t row_stride, const int64_t* lo,
+                                  const int64_t* hi, int32_t n_win, int32_t* out_ids, void* workspace,
+                                  const WsLayout& l, int sms, cudaStream_t stream);
+
 cudaError_t launch_rows_argmax(int dtype, const void* window_base, int64_t rows, int64_t width, int64_t row_stride,
                                int64_t lo, int32_t* out_ids, int sms, cudaStream_t stream);
 
@@ -99,6 +117,8 @@ constexpr int kMaxHistory = LOOM_SELECT_MAX_HISTORY;
 constexpr int kSampleCtasPerSm = 2;  // the sampler runs two CTAs per SM
 
 size_t sample_record_bytes(int32_t top_k);
+// The sampler's grid for a call (every sampling entry point launches this one).
+inline int sample_ctas(int64_t rows, int64_t width, int sms) { return stream_ctas(rows, width, kSampleCtasPerSm * sms); }
 cudaError_t launch_sample_stream(const SampleLaunch& a, void* workspace, const WsLayout& l, int ctas,
                                  cudaStream_t stream);
 cudaError_t launch_shard_merge(const void* records, int32_t n_shards, int64_t rows, const float* u, int32_t top_k,

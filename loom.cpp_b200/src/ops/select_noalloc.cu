@@ -28,12 +28,14 @@
 namespace loom_select {
 namespace {
 
-// status word + tickets + 2 records per CTA of 16 + 8 * 64 bytes (the sampler's layout at top_k 64)
+// status word + tickets + the (unused here) pair region + 2 records per CTA of 16 + 8 * 64 bytes: the
+// sampler's workspace layout (ws_layout) at top_k 64
 constexpr size_t kNoAllocRecordBytes = 16 + 8 * LOOM_SELECT_NOALLOC_MAX_TOP_K;
 constexpr size_t kNoAllocTicketBytes = ((kTicketSlots * sizeof(int32_t) + kWsAlign - 1) / kWsAlign) * kWsAlign;
+constexpr size_t kNoAllocPairBytes = ((kChunkPairs * kChunkPairBytes + kWsAlign - 1) / kWsAlign) * kWsAlign;
 constexpr size_t kNoAllocRecordsBytes =
     ((kNoAllocRecordBytes * kStreamRecordSlots + kWsAlign - 1) / kWsAlign) * kWsAlign;
-constexpr size_t kNoAllocScratchBytes = kWsAlign + kNoAllocTicketBytes + kNoAllocRecordsBytes;
+constexpr size_t kNoAllocScratchBytes = kWsAlign + kNoAllocTicketBytes + kNoAllocPairBytes + kNoAllocRecordsBytes;
 static_assert(kNoAllocScratchBytes == LOOM_SELECT_NOALLOC_SCRATCH_BYTES, "header constant out of date");
 
 // The scratch. In host code this name is only a stand-in for the device array: its device address
@@ -115,7 +117,7 @@ extern "C" int loom_sample_rows_noalloc(const void* logits, int dtype, int64_t r
     const WsLayout l = ws_layout(sample_record_bytes(params->top_k), kStreamRecordSlots);
     if (l.bytes > kNoAllocScratchBytes) return LOOM_SELECT_ESHAPE;
     // the grid loom_sample_rows would launch for the same call
-    const int ctas = stream_ctas(rows, n_vocab, kSampleCtasPerSm * sms);
+    const int ctas = sample_ctas(rows, n_vocab, sms);
     if (launch_sample_stream(a, scratch, l, ctas, st) != cudaSuccess) return LOOM_SELECT_ECUDA;
     // the device-side status word (history ids out of range, a timed-out wait) for the caller
     if (out_status && cudaMemcpyAsync(out_status, scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)

@@ -211,7 +211,7 @@ __device__ __forceinline__ float tempered(float x, float T, bool greedy) { retur
 // computed below, so filtering on x >= X drops only elements that tempered(x) < t rules out. It
 // starts a few ulps under t * T and checks that tempered(X) < t (then X lies below the exact
 // boundary by monotonicity); one or two divides instead of a search.
-__device__ float inverse_threshold(float t, float T, bool greedy);
+__device__ inline float inverse_threshold(float t, float T, bool greedy);
 
 __device__ __forceinline__ float inverse_threshold_bound(float t, float T, bool greedy) {
     if (greedy || t == -__int_as_float(0x7f800000)) return t;
@@ -230,7 +230,7 @@ __device__ __forceinline__ float inverse_threshold_bound(float t, float T, bool 
 // The smallest float x with tempered(x) >= t (t not NaN): every x below it has tempered(x) < t.
 // Division by T > 0 in round-to-nearest is monotone, so a search over ordinals finds it exactly:
 // gallop from the estimate t * T to bracket the boundary, then bisect.
-__device__ float inverse_threshold(float t, float T, bool greedy) {
+__device__ inline float inverse_threshold(float t, float T, bool greedy) {
     if (greedy) return t;
     if (t == -__int_as_float(0x7f800000)) return t;
     // predicate(o) = tempered(ordinal_to_float(o)) >= t; false at -inf (t > -inf), true at +inf
@@ -277,7 +277,7 @@ __device__ float inverse_threshold(float t, float T, bool greedy) {
 // The survivor decision on keys sorted best-first, by warp 0 only (the other threads skip it):
 // weights, sequential prefix sums, top-p cutoff and draw, exactly as the oracle orders them.
 // e and S are scratch arrays of K doubles.
-__device__ void decide_warp(const uint64_t* keys, int K, float top_p, float u, double* e, double* S, int32_t* id_out,
+__device__ inline void decide_warp(const uint64_t* keys, int K, float top_p, float u, double* e, double* S, int32_t* id_out,
                             float* prob_out, float* y_out) {
     const int lane = threadIdx.x & 31;
     const float m = rank_key_value(keys[0]);
