@@ -95,6 +95,8 @@ struct SampleShared {
     unsigned long long key_t;  // warp path: every kept key reaches this (a k-th best key, or a value floor)
     uint32_t x_key;            // warp path: order key of the raw threshold X
     float wq[kSampWarps];      // warp path: per warp, a raw value that ceil(k / warps) of its lanes' maxima reach
+    int mcnt[32];              // split-row merge: the batch's piece counts (-1: a bad history id)
+    LseAcc mpart[32];          // and their log-sum-exp states
 };
 
 __device__ __forceinline__ float neg_inf() { return -__int_as_float(0x7f800000); }
@@ -359,28 +361,47 @@ __device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segm
     group_sync<kNT>();
     if (!sh->last) return;
     __threadfence();
-    // merge every piece's record
-    int have = 0;
+    // merge every piece's record, in batches of up to 32 pieces whose loads are in flight together:
+    // piece b's k key slots go to cand[have + b k, have + (b + 1) k), those past its count as 0
+    // (below every real key; the number of real keys bounds the result)
+    const int fit = (kCap - p.k) / p.k;
+    const int per_batch = fit < 1 ? 1 : (fit > 32 ? 32 : fit);
+    int have = 0, real = 0;
     bool any_bad = false;
     LseAcc tot = lse_init();
-    for (int j = 0; j < s.count; ++j) {
-        const unsigned char* r = p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j, s.row)) * p.rec_bytes;
-        const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
-        if (c < 0) {
-            any_bad = true;
-            continue;
+    for (int j0 = 0; j0 < s.count; j0 += per_batch) {
+        const int nb = s.count - j0 < per_batch ? s.count - j0 : per_batch;
+        if (have + nb * p.k > kCap) have = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
+        for (int idx = tid; idx < nb * p.k; idx += kNT) {
+            const int bb = idx / p.k, i = idx - bb * p.k;
+            const unsigned char* r =
+                p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j0 + bb, s.row)) * p.rec_bytes;
+            const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
+            const uint64_t key = __ldcg(reinterpret_cast<const uint64_t*>(r + 16) + i);
+            cand[have + idx] = i < c ? key : 0ull;
         }
-        LseAcc part;
-        part.m = __ldcg(reinterpret_cast<const float*>(r) + 1);
-        part.s = __ldcg(reinterpret_cast<const float*>(r) + 2);
-        tot = lse_merge(tot, part);
-        if (have + c > kCap) have = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
-        const uint64_t* rk = reinterpret_cast<const uint64_t*>(r + 16);
-        for (int i = tid; i < c; i += kNT) cand[have + i] = __ldcg(rk + i);
-        have += c;
+        if (tid < nb) {
+            const unsigned char* r =
+                p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j0 + tid, s.row)) * p.rec_bytes;
+            sh->mcnt[tid] = __ldcg(reinterpret_cast<const int32_t*>(r));
+            sh->mpart[tid].m = __ldcg(reinterpret_cast<const float*>(r) + 1);
+            sh->mpart[tid].s = __ldcg(reinterpret_cast<const float*>(r) + 2);
+        }
         group_sync<kNT>();
+        for (int bb = 0; bb < nb; ++bb) {  // every thread, in the same order: the same results
+            const int c = sh->mcnt[bb];
+            if (c < 0) {
+                any_bad = true;
+            } else {
+                tot = lse_merge(tot, sh->mpart[bb]);
+                real += c;
+            }
+        }
+        have += nb * p.k;
+        group_sync<kNT>();  // mcnt / mpart are rewritten by the next batch
     }
-    const int Kf = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
+    int Kf = select_best<kNT, kCap, kSmallK>(cand, have, p.k, &sh->tk);
+    if (Kf > real) Kf = real;
     if (tid == 0) p.tickets[record_slot(g, s.first_cta, s.row)] = 0;
     finalize_row<kDtype, kNT>(p, g, s.row, cand, e, S, Kf, tot, any_bad, sh);
 }
@@ -672,6 +693,16 @@ static_assert(kWarpKeyCap <= 256, "a warp sorts at most 8 keys per lane");
 static_assert(2 * kWarpMaxK * sizeof(double) <= kSampWarps * kWarpKeyCap * sizeof(uint64_t),
               "decision scratch fits the key buffers");
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
+
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
@@ -742,7 +773,7 @@ __device__ int warp_keep_best(uint64_t* w, int n, int k) {
     return warp_keep_best_p<8>(w, n, k);
 }
 
-template <int kDtype>
+template <int kDtype, bool kLse>
 struct WarpSampleOp {
     static constexpr int kEsz = (kDtype == LOOM_SELECT_BF16) ? 2 : 4;
     static constexpr int kPer = 16 / kEsz;
@@ -763,6 +794,94 @@ struct WarpSampleOp {
     float tv;      // this lane's entry of the warp's sorted list of stage maxima (lane i: i-th largest)
     float wv;      // the list's ceil(k / warps)-th entry
     bool pending;  // wv has risen since it was last published
+    float lm, ls;     // log-sum-exp of the streamed elements in raw units: max lm, ls = sum of 2^((x - lm) c)
+    float c;          // log2(e) / T (log2(e) for greedy rows)
+    uint32_t* wflag;  // this warp's 32 words: per lane, which of its vectors of the stage hold a history id
+
+    // One value into the lane's raw-unit log-sum-exp (NaN and -inf add nothing).
+    __device__ __forceinline__ void raw_offer(float v) {
+        if (v != v || v == neg_inf()) return;
+        if (v > lm) {
+            ls = ls * ex2_approx(__fmul_rn(__fsub_rn(lm, v), c)) + 1.0f;
+            lm = v;
+        } else if (v == lm) {
+            ls += 1.0f;
+        } else {
+            ls += ex2_approx(__fmul_rn(__fsub_rn(v, lm), c));
+        }
+    }
+
+    // Log-sum-exp terms of this lane's vectors of a stage, in raw units. History ids are left out
+    // (they enter at their penalised value at the segment end): the warp first flags, from the
+    // segment's list of distinct ids, the vectors of its lanes that hold one. A flagged vector goes
+    // element by element; every other one costs two float operations and one ex2 per element,
+    // after one rescale to the largest of their maxima.
+    template <int kV>
+    __device__ void lse_stage(const uint4* v4, int32_t nvec, int64_t gid0, const float (&mu)[kV]) {
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        uint32_t fl = 0u;
+        const int nu = p.penalty ? sh->n_uniq : 0;
+        if (nu > 0) {
+            const int64_t n = static_cast<int64_t>(nvec) * kPer;
+            for (int j = lane; j < nu; j += 32) {
+                const int64_t e = static_cast<int64_t>(uniq[j]) - gid0;
+                if (e >= 0 && e < n) {
+                    const int32_t v = static_cast<int32_t>(e / kPer);
+                    if (((v % kNT) >> 5) == warp) atomicOr(&wflag[v & 31], 1u << (v / kNT));
+                }
+            }
+            __syncwarp();
+            fl = wflag[lane];
+            wflag[lane] = 0u;
+            __syncwarp();
+        }
+        float smc = neg_inf();
+#pragma unroll
+        for (int i = 0; i < kV; ++i)
+            if (!((fl >> i) & 1u)) smc = fmaxf(smc, mu[i]);  // (a vector past the stage's end has NaN)
+        const float mnew = fmaxf(lm, smc);
+        if (mnew > lm) {
+            ls = ls * ex2_approx(__fmul_rn(__fsub_rn(lm, mnew), c));
+            lm = mnew;
+        }
+        if (lm == pos_inf()) {
+#pragma unroll
+            for (int i = 0; i < kV; ++i) {
+                const int32_t v = i * kNT + tid;
+                if (v < nvec && !((fl >> i) & 1u)) {
+                    Vec16<kDtype> e;
+                    e.unpack(v4[v]);
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q) ls += e.x[q] == pos_inf() ? 1.0f : 0.0f;
+                }
+            }
+        } else if (lm > neg_inf()) {
+            const float m = lm;
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kV; ++i) {
+                const int32_t v = i * kNT + tid;
+                if (v < nvec && !((fl >> i) & 1u)) {
+                    Vec16<kDtype> e;
+                    e.unpack(v4[v]);
+#pragma unroll
+                    for (int q = 0; q < kPer; ++q)
+                        sum += ex2_approx(fmaxf(__fmul_rn(__fsub_rn(e.x[q], m), c), neg_inf()));
+                }
+            }
+            ls += sum;
+        }
+        while (fl) {
+            const int i = __ffs(fl) - 1;
+            fl &= fl - 1u;
+            const int32_t v = i * kNT + tid;
+            Vec16<kDtype> e;
+            e.unpack(v4[v]);
+#pragma unroll
+            for (int q = 0; q < kPer; ++q)
+                if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q)) raw_offer(e.x[q]);
+        }
+    }
 
     __device__ const unsigned char* row_ptr(int64_t row) const { return g.base + row * g.row_stride * kEsz; }
     __device__ const int32_t* row_hist(int64_t row) const { return p.hist + row * static_cast<int64_t>(p.hist_len); }
@@ -876,6 +995,8 @@ struct WarpSampleOp {
             for (int w = 0; w < kSampWarps; ++w) sh->wq[w] = neg_inf();
         }
         lse = lse_init();
+        lm = neg_inf();
+        ls = 0.0f;
         nr = 0;
         nk = 0;
         stage = 0;
@@ -907,9 +1028,11 @@ struct WarpSampleOp {
                 const int64_t col = segment_edge_col(s, kEsz, lane);
                 x = load_global_elem<kDtype>(row_ptr(s.row), col);
                 gid = static_cast<int32_t>(p.vocab_offset + col);
-                if (is_history(gid)) x = penalise(x, p.r);
-                if (p.lse) lse_offer(lse, tempered(x, p.T, p.greedy));
-                take = x == x;
+                // a history id enters at the segment end, with the segment's other history ids
+                if (!is_history(gid)) {
+                    if (p.lse) lse_offer(lse, tempered(x, p.T, p.greedy));
+                    take = x == x;
+                }
             }
             append(take, x, gid);
         }
@@ -972,7 +1095,7 @@ struct WarpSampleOp {
         static_assert(kVecsPerThread <= 32, "marks are one 32-bit word");
         float mu[kVecsPerThread];
         float smax = neg_inf();
-        if (nvec == kVecsPerThread * kNT && !p.lse) {
+        if (nvec == kVecsPerThread * kNT) {
 #pragma unroll
             for (int i = 0; i < kVecsPerThread; ++i) {
                 mu[i] = vec_max<kDtype>(v4[i * kNT + tid]);
@@ -983,21 +1106,11 @@ struct WarpSampleOp {
             for (int i = 0; i < kVecsPerThread; ++i) {
                 const int32_t v = i * kNT + tid;
                 mu[i] = __int_as_float(0x7fc00000);
-                if (v < nvec) {
-                    Vec16<kDtype> e;
-                    e.unpack(v4[v]);
-                    mu[i] = vec_max<kDtype>(v4[v]);
-                    if (p.lse) {
-                        // every element once (history ids are offered at the segment end)
-#pragma unroll
-                        for (int q = 0; q < kPer; ++q)
-                            if (!is_history(gid0 + static_cast<int64_t>(v) * kPer + q))
-                                lse_offer(lse, tempered(e.x[q], p.T, p.greedy));
-                    }
-                }
+                if (v < nvec) mu[i] = vec_max<kDtype>(v4[v]);
                 smax = fmaxf(smax, mu[i]);
             }
         }
+        if constexpr (kLse) lse_stage<kVecsPerThread>(v4, nvec, gid0, mu);
         uint32_t hits = 0;
         if (smax >= X) {
 #pragma unroll
@@ -1062,6 +1175,13 @@ struct WarpSampleOp {
     __device__ void end_segment(const Segment& s) {
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
         prune();  // at most k keys per warp, the raw buffer empty
+        if (kLse && ls > 0.0f) {
+            // the streamed sum, relative to the tempered maximum: 2^((x - lm) c) = e^(x / T - lm / T)
+            LseAcc r;
+            r.m = tempered(lm, p.T, p.greedy);
+            r.s = ls;
+            lse = lse_merge(lse, r);
+        }
         if (p.penalty) {
             // The segment's distinct history ids with their penalised, tempered values, read from
             // global memory (the row has just streamed through L2), against the final threshold.
@@ -1110,10 +1230,12 @@ struct WarpSampleOp {
 
 constexpr size_t kWarpDynSmem = static_cast<size_t>(kWarpStages) * kWarpStageBytes +
                                 kSampWarps * kRawCap * sizeof(uint2) + kSampWarps * kWarpKeyCap * sizeof(uint64_t) +
-                                kHashSlots * sizeof(int32_t) + kMaxHistory * sizeof(int32_t);
+                                kHashSlots * sizeof(int32_t) + kMaxHistory * sizeof(int32_t) +
+                                kSampWarps * 32 * sizeof(uint32_t);
 static_assert(kWarpDynSmem + 4096 <= 232448 / kSampCtasPerSm, "two CTAs per SM must fit the SM's shared memory");
 
-template <int kDtype>
+// kLse: the log-sum-exp is wanted (log-probabilities or shard records), p.lse == kLse.
+template <int kDtype, bool kLse>
 __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_stream_kernel(StreamGeom g, SampleDev p) {
     extern __shared__ __align__(128) unsigned char dyn[];
     __shared__ StreamCtl ctl;
@@ -1123,11 +1245,16 @@ __global__ void __launch_bounds__((kSampWarps + 1) * 32, kSampCtasPerSm) sample_
     uint64_t* keys_all = reinterpret_cast<uint64_t*>(raw_all + kSampWarps * kRawCap);
     int32_t* hset = reinterpret_cast<int32_t*>(keys_all + kSampWarps * kWarpKeyCap);
     int32_t* uniq = hset + kHashSlots;
+    uint32_t* wflag_all = reinterpret_cast<uint32_t*>(uniq + kMaxHistory);
+    // (zeroed before the streamer's first barrier; each stage's reader returns its words to zero)
+    for (int i = threadIdx.x; i < kSampWarps * 32; i += blockDim.x) wflag_all[i] = 0u;
     const int warp = threadIdx.x >> 5;
     const int w = warp < kSampWarps ? warp : 0;  // the producer warp holds no buffers
-    WarpSampleOp<kDtype> op{g,     p,    &sh,  raw_all + w * kRawCap, keys_all + w * kWarpKeyCap,
-                            reinterpret_cast<uint64_t*>(raw_all), keys_all, hset, uniq, lse_init(), 0, 0, 0,
-                            neg_inf(), neg_inf(), false};  // (tv, wv, pending)
+    const float c = p.greedy ? kLog2e : __fdiv_rn(kLog2e, p.T);
+    WarpSampleOp<kDtype, kLse> op{g,     p,    &sh,  raw_all + w * kRawCap, keys_all + w * kWarpKeyCap,
+                                  reinterpret_cast<uint64_t*>(raw_all), keys_all, hset, uniq, lse_init(), 0, 0, 0,
+                                  neg_inf(), neg_inf(), false,            // (tv, wv, pending)
+                                  neg_inf(), 0.0f, c, wflag_all + w * 32};  // (lm, ls, c, wflag)
     stream_ranges_warps<kWarpStages, kWarpStageBytes, kSampWarps>(g, op, ring, &ctl, p.status);
 }
 
@@ -1211,16 +1338,21 @@ cudaError_t launch_sample_t(const StreamGeom& g, const SampleDev& p, cudaStream_
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(sample_stream_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kWarpDynSmem));
+        cudaError_t e = cudaFuncSetAttribute(sample_stream_kernel<kDtype, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kWarpDynSmem));
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(sample_stream_kernel<kDtype, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kWarpDynSmem));
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(sample_wide_kernel<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kWideDynSmem));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    if (p.k <= kWarpMaxK)
-        sample_stream_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kWarpDynSmem, stream>>>(g, p);
+    if (p.k <= kWarpMaxK && p.lse)
+        sample_stream_kernel<kDtype, true><<<g.ctas, (kSampWarps + 1) * 32, kWarpDynSmem, stream>>>(g, p);
+    else if (p.k <= kWarpMaxK)
+        sample_stream_kernel<kDtype, false><<<g.ctas, (kSampWarps + 1) * 32, kWarpDynSmem, stream>>>(g, p);
     else
         sample_wide_kernel<kDtype><<<g.ctas, (kSampWarps + 1) * 32, kWideDynSmem, stream>>>(g, p);
     return cudaGetLastError();
