@@ -362,8 +362,9 @@ __device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segm
     if (!sh->last) return;
     __threadfence();
     // merge every piece's record, in batches of up to 32 pieces whose loads are in flight together:
-    // piece b's k key slots go to cand[have + b k, have + (b + 1) k), those past its count as 0
-    // (below every real key; the number of real keys bounds the result)
+    // piece b's k key slots go to cand[have + b k, have + (b + 1) k), those past its count as a
+    // filler key (piece index * k + slot + 1: below 2^32, so below every real key, and distinct, as
+    // the selection needs); the number of real keys bounds the result
     const int fit = (kCap - p.k) / p.k;
     const int per_batch = fit < 1 ? 1 : (fit > 32 ? 32 : fit);
     int have = 0, real = 0;
@@ -378,7 +379,7 @@ __device__ void finish_segment(const SampleDev p, const StreamGeom g, const Segm
                 p.recs + static_cast<size_t>(record_slot(g, s.first_cta + j0 + bb, s.row)) * p.rec_bytes;
             const int32_t c = __ldcg(reinterpret_cast<const int32_t*>(r));
             const uint64_t key = __ldcg(reinterpret_cast<const uint64_t*>(r + 16) + i);
-            cand[have + idx] = i < c ? key : 0ull;
+            cand[have + idx] = i < c ? key : static_cast<uint64_t>(j0) * p.k + idx + 1;
         }
         if (tid < nb) {
             const unsigned char* r =
