@@ -100,6 +100,18 @@ LOOM_SELECT_API int loom_select_workspace_init(void* workspace, size_t workspace
 LOOM_SELECT_API int loom_select_read_status(void* workspace, void* stream);
 
 /*
+ * Test hook, no loom.cpp counterpart: drives the bounded-wait failure path of the streamed kernels
+ * (argmax of long rows, the sampler for top_k <= 128) without any fault. It writes into the
+ * workspace header, on `stream`: wait_limit_ns (> 0) replaces the 2 s bound of every wait of those
+ * kernels, and withhold_stage >= 0 makes the first CTA's producer leave that stage of its range
+ * unissued, so its consumers' waits run out. The next such call records LOOM_SELECT_ETIMEOUT (its
+ * outputs are invalid) and every wait still ends. loom_select_workspace_init clears the hook and
+ * the state a timed-out call leaves behind; nothing else touches it. Not for production use.
+ */
+LOOM_SELECT_API int loom_select_test_wait_fault(void* workspace, int64_t wait_limit_ns, int32_t withhold_stage,
+                                                void* stream);
+
+/*
  * Greedy argmax of every row over the id window [lo, hi), hi < 0 meaning n_vocab.
  *
  * Replaces Generator::argmax (src/core/generation.cpp:64-74) and the scan inside argmax_tensor_row /

@@ -48,6 +48,7 @@ EXPORTS = (
     "loom_ctc_workspace_size",
     "loom_select_workspace_init",
     "loom_select_read_status",
+    "loom_select_test_wait_fault",
     "loom_argmax_rows",
     "loom_argmax_windows_workspace_size",
     "loom_argmax_windows",
@@ -94,6 +95,7 @@ def _lib():
             "loom_ctc_workspace_size": (sz, [i64, i64]),
             "loom_select_workspace_init": (ctypes.c_int, [vp, sz, vp]),
             "loom_select_read_status": (ctypes.c_int, [vp, vp]),
+            "loom_select_test_wait_fault": (ctypes.c_int, [vp, i64, i32, vp]),
             "loom_argmax_rows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
             "loom_argmax_windows_workspace_size": (sz, [i64, i32]),
             "loom_argmax_windows": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, vp, vp, i32, vp, vp, sz, vp]),

@@ -156,6 +156,19 @@ int loom_select_read_status(void* workspace, void* stream) {
     return value;
 }
 
+int loom_select_test_wait_fault(void* workspace, int64_t wait_limit_ns, int32_t withhold_stage, void* stream) {
+    if (!workspace) return LOOM_SELECT_EWORKSPACE;
+    if (wait_limit_ns <= 0 || withhold_stage < -1) return LOOM_SELECT_EINVAL;
+    // the header layout read by read_wait_fault (select_device.cuh): bytes [8, 16) and [16, 20)
+    struct {
+        uint64_t limit_ns;
+        int32_t withhold;
+    } hdr{static_cast<uint64_t>(wait_limit_ns), withhold_stage + 1};
+    // (pageable source: the copy has read it before this returns)
+    return map_cuda(cudaMemcpyAsync(static_cast<unsigned char*>(workspace) + 8, &hdr, 12, cudaMemcpyHostToDevice,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
 int loom_argmax_rows(const void* logits, int dtype, int64_t rows, int64_t n_vocab, int64_t row_stride, int64_t lo,
                      int64_t hi, int32_t* out_ids, void* workspace, size_t workspace_bytes, void* stream) {
     if (!dtype_ok(dtype)) return LOOM_SELECT_EDTYPE;

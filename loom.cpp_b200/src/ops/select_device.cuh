@@ -23,6 +23,23 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// Test hook in the workspace header (written only by loom_select_test_wait_fault; zero otherwise):
+// bytes [8, 16) a wait limit in ns replacing kWaitLimitNs (0: the default), bytes [16, 20) the
+// index of one stage that CTA 0's producer of a streamed kernel leaves unissued (0: none; the value
+// is the index + 1), so that the consumers' bounded waits run out.
+struct WaitFault {
+    uint64_t limit_ns;
+    int32_t withhold;  // stage index + 1, or 0
+};
+
+__device__ __forceinline__ WaitFault read_wait_fault(const int* status_word) {
+    WaitFault f;
+    const uint64_t lim = *reinterpret_cast<const volatile uint64_t*>(status_word + 2);
+    f.limit_ns = lim ? lim : kWaitLimitNs;
+    f.withhold = *reinterpret_cast<const volatile int32_t*>(status_word + 4);
+    return f;
+}
+
 // Records the first device-side error of a call in the workspace status word.
 __device__ __forceinline__ void record_status(int* status_word, int code) {
     atomicCAS(status_word, 0, code);
@@ -75,12 +92,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Waits for the phase of `bar` with the given parity to complete; false (and a recorded timeout)
 // if it does not within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
         if (mbar_try_wait_sleep(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit_ns) {
             record_status(status_word, LOOM_SELECT_ETIMEOUT);
             return false;
         }

@@ -125,6 +125,8 @@ struct StreamCtl {
     int issued;
     int consumed;
     int waited[16];  // stream_ranges_warps: stages each consumer warp saw land
+    uint64_t limit_ns;  // stream_ranges_warps: the bound of every wait (see WaitFault)
+    int withhold;       // stream_ranges_warps: a stage CTA 0 leaves unissued (index + 1), or 0
 };
 
 // The persistent CTA body. Consumers are warps [0, kConsumerWarps); warp kConsumerWarps produces.
@@ -239,7 +241,8 @@ __device__ void stream_ranges(const StreamGeom g, Op& op, unsigned char* ring, S
 // Waits, as a whole warp, for the phase of `bar` with the given parity: every lane polls the barrier
 // (so each lane has the barrier's acquire), lane 0's clock and the abort flag decide for the warp.
 // False when the wait runs out (recorded as LOOM_SELECT_ETIMEOUT) or another warp has aborted.
-__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word, const int* abort) {
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, int* status_word, const int* abort,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
@@ -247,7 +250,7 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
         int give_up = 0;
         if ((threadIdx.x & 31) == 0) {
             if (*reinterpret_cast<const volatile int*>(abort)) give_up = 1;
-            else if (global_timer_ns() - t0 > kWaitLimitNs) give_up = 2;
+            else if (global_timer_ns() - t0 > limit_ns) give_up = 2;
         }
         give_up = __shfl_sync(0xffffffffu, give_up, 0);
         if (give_up) {
@@ -258,13 +261,14 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // mbar_wait_bounded for one thread that also gives up once another warp has aborted.
-__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int* status_word, const int* abort) {
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int* status_word, const int* abort,
+                                                    uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
         if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*reinterpret_cast<const volatile int*>(abort)) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit_ns) {
             record_status(status_word, LOOM_SELECT_ETIMEOUT);
             return false;
         }
@@ -298,6 +302,9 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
         ctl->abort = 0;
         ctl->issued = 0;
         ctl->consumed = 0;
+        const WaitFault f = read_wait_fault(status);
+        ctl->limit_ns = f.limit_ns;
+        ctl->withhold = blockIdx.x == 0 ? f.withhold : 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -317,7 +324,7 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
                 const uint32_t parity = ((it / kStages) & 1) ^ 1;
                 int ok = 1;
                 if (lane == 0) {
-                    ok = mbar_wait_abortable(&ctl->empty[slot], parity, status, &ctl->abort) ? 1 : 0;
+                    ok = mbar_wait_abortable(&ctl->empty[slot], parity, status, &ctl->abort, ctl->limit_ns) ? 1 : 0;
                     if (!ok) atomicExch(&ctl->abort, 1);
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -325,7 +332,7 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
                     stop = true;
                     break;
                 }
-                if (lane == 0) {
+                if (lane == 0 && it + 1 != ctl->withhold) {  // (the test hook leaves one stage unissued)
                     const unsigned char* src = s.A0 + static_cast<int64_t>(k) * kStageBytes;
                     const int64_t left = s.A1 - src;
                     const uint32_t bytes = static_cast<uint32_t>(left < kStageBytes ? left : kStageBytes);
@@ -348,7 +355,7 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
                 const int slot = it % kStages;
                 const uint32_t parity = (it / kStages) & 1;
                 if (live) {
-                    live = warp_wait_bounded(&ctl->full[slot], parity, status, &ctl->abort);
+                    live = warp_wait_bounded(&ctl->full[slot], parity, status, &ctl->abort, ctl->limit_ns);
                     if (live) waited = it + 1;
                     else if (lane == 0) atomicExch(&ctl->abort, 1);
                 }
@@ -376,7 +383,8 @@ __device__ void stream_ranges_warps(const StreamGeom g, Op& op, unsigned char* r
         int from = ctl->issued;
         for (int w = 0; w < kConsumerWarps; ++w) from = ctl->waited[w] < from ? ctl->waited[w] : from;
         for (int i = from; i < ctl->issued; ++i) {
-            if (!mbar_wait_bounded(&ctl->full[i % kStages], (i / kStages) & 1, status)) break;
+            if (i + 1 == ctl->withhold) continue;  // never issued
+            if (!mbar_wait_bounded(&ctl->full[i % kStages], (i / kStages) & 1, status, ctl->limit_ns)) break;
         }
     }
     __syncthreads();
