@@ -95,6 +95,7 @@ struct SampleShared {
     unsigned long long key_t;  // warp path: every kept key reaches this (a k-th best key, or a value floor)
     uint32_t x_key;            // warp path: order key of the raw threshold X
     float wq[kSampWarps];      // warp path: per warp, a raw value that ceil(k / warps) of its lanes' maxima reach
+    float u_row;               // the segment's row's uniform (loaded when the segment starts)
     int mcnt[32];              // split-row merge: the batch's piece counts (-1: a bad history id)
     LseAcc mpart[32];          // and their log-sum-exp states
 };
@@ -307,7 +308,7 @@ __device__ void finalize_row(const SampleDev p, const StreamGeom g, int64_t row,
                 sh->sel_prob = 1.0f;
             }
         } else {
-            decide_warp(cand, K, p.p, __ldg(p.u + row), e, S, &sh->sel_id, &sh->sel_prob, &sh->sel_y);
+            decide_warp(cand, K, p.p, sh->u_row, e, S, &sh->sel_id, &sh->sel_prob, &sh->sel_y);
         }
         if (lane == 0) {
             p.out_ids[row] = sh->sel_id;
@@ -435,6 +436,7 @@ struct WideSampleOp {
         const int tid = threadIdx.x;
         if (tid == 0) {
             sh->K = 0;
+            if (p.u && !p.shard && !p.greedy) sh->u_row = __ldg(p.u + s.row);  // used at the row's end
             sh->fail = 0;
             sh->bad = 0;
             sh->n_uniq = 0;
@@ -988,6 +990,7 @@ struct WarpSampleOp {
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
         if (tid == 0) {
             sh->K = 0;
+            if (p.u && !p.shard && !p.greedy) sh->u_row = __ldg(p.u + s.row);  // used at the row's end
             sh->bad = 0;
             sh->n_uniq = 0;
             sh->warm_key = 0xffffffffu;
