@@ -515,8 +515,12 @@ def run_decode(args, sel, synth, torch, dev, rank, world, cpu):
     want = ob.argmax_rows(rows.cpu().numpy(), nthreads=os.cpu_count() or 1)
     ok = bool(np.array_equal(ids_a, want)) and (ids_g is None or bool(np.array_equal(ids_g, want)))
     res = {"config": "greedy argmax, [1, 151936] f32 N(0, 3^2) + 8 spikes of +10, 512 steps (one row each)",
-           "device_us_per_step": dev_us, "decode_loop_us_per_step": loop_us,
-           "graph_us_per_step": graph_us, "steps": DECODE_STEPS, "parity_ok": all_true(ok, world)}
+           "device_us_per_step": graph_us if isinstance(graph_us, float) else None,
+           "device_time": "the 512 steps as one CUDA graph, replayed (no host launch gaps)",
+           "launch_us_per_step": dev_us,
+           "launch_time": "events around each launch from Python: bound by the host's launch rate",
+           "decode_loop_us_per_step": loop_us, "graph_us_per_step": graph_us, "steps": DECODE_STEPS,
+           "parity_ok": all_true(ok, world)}
     if cpu:
         got = np.zeros(DECODE_STEPS, dtype=np.int32)
         secs = ob.refpath_lib().refpath_greedy_decode(rows.data_ptr(), DECODE_STEPS, VOCAB, VOCAB,
