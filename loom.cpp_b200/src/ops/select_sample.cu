@@ -704,6 +704,22 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 __device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
 
+// (a0, a1) - (m, m), then * (c, c): two packed f32x2 operations, each element rounded as the
+// scalar __fsub_rn / __fmul_rn would round it. mm and cc hold (m, m) and (c, c).
+__device__ __forceinline__ void sub_mul_f32x2(float a0, float a1, uint64_t mm, uint64_t cc, float& d0, float& d1) {
+    uint64_t a, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(mm));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(d), "l"(cc));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+__device__ __forceinline__ uint64_t f32x2_splat(float v) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+    return r;
+}
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -859,8 +875,11 @@ struct WarpSampleOp {
                 }
             }
         } else if (lm > neg_inf()) {
+            // -inf elements give 2^-inf = 0; a NaN element makes the sum NaN, and only then is the
+            // stage summed again with each term guarded
             const float m = lm;
-            float sum = 0.0f;
+            const uint64_t mm = f32x2_splat(m), cc = f32x2_splat(c);
+            float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
             for (int i = 0; i < kV; ++i) {
                 const int32_t v = i * kNT + tid;
@@ -868,8 +887,27 @@ struct WarpSampleOp {
                     Vec16<kDtype> e;
                     e.unpack(v4[v]);
 #pragma unroll
-                    for (int q = 0; q < kPer; ++q)
-                        sum += ex2_approx(fmaxf(__fmul_rn(__fsub_rn(e.x[q], m), c), neg_inf()));
+                    for (int q = 0; q < kPer; q += 2) {
+                        float d0, d1;
+                        sub_mul_f32x2(e.x[q], e.x[q + 1], mm, cc, d0, d1);
+                        s0 += ex2_approx(d0);
+                        s1 += ex2_approx(d1);
+                    }
+                }
+            }
+            float sum = s0 + s1;
+            if (sum != sum) {
+                sum = 0.0f;
+#pragma unroll
+                for (int i = 0; i < kV; ++i) {
+                    const int32_t v = i * kNT + tid;
+                    if (v < nvec && !((fl >> i) & 1u)) {
+                        Vec16<kDtype> e;
+                        e.unpack(v4[v]);
+#pragma unroll
+                        for (int q = 0; q < kPer; ++q)
+                            sum += ex2_approx(fmaxf(__fmul_rn(__fsub_rn(e.x[q], m), c), neg_inf()));
+                    }
                 }
             }
             ls += sum;
