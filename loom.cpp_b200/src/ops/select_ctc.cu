@@ -59,14 +59,6 @@ struct CtcShared {
 // Frames are split evenly: CTA c owns [c * total / G, (c + 1) * total / G).
 __device__ __forceinline__ int64_t ctc_range_start(int64_t c, int64_t total, int64_t G) { return c * total / G; }
 
-__device__ __forceinline__ int64_t ctc_cta_of_frame(int64_t f, int64_t total, int64_t G) {
-    int64_t c = f * G / total;
-    if (c >= G) c = G - 1;
-    while (c + 1 < G && ctc_range_start(c + 1, total, G) <= f) ++c;
-    while (c > 0 && ctc_range_start(c, total, G) > f) --c;
-    return c;
-}
-
 // Compacts utterance u's kept frames. Called by the whole CTA. Each thread takes kCollapsePer
 // consecutive frames (their ids loaded at once), and one block scan per pass places the kept ones.
 constexpr int kCollapsePer = 8;
@@ -74,10 +66,11 @@ constexpr int kCollapsePer = 8;
 __device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const int32_t* frame_ids, int32_t* out_ids,
                              int32_t* out_frames, int32_t* out_len, CtcShared* sh) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool act = threadIdx.x < kRowNT;  // a CTA's further warps (a producer) only meet the barriers
     const int32_t* ids = frame_ids + u * n_frames;
     int carry = 0;  // frames kept by the earlier passes (the same in every thread)
     for (int64_t base = 0; base < n_frames; base += static_cast<int64_t>(kRowNT) * kCollapsePer) {
-        const int64_t f0 = base + static_cast<int64_t>(threadIdx.x) * kCollapsePer;
+        const int64_t f0 = act ? base + static_cast<int64_t>(threadIdx.x) * kCollapsePer : n_frames + 1;
         int32_t v[kCollapsePer];
         const int32_t prev0 = (f0 == 0 || f0 > n_frames) ? blank : __ldcg(ids + f0 - 1);
 #pragma unroll
@@ -95,7 +88,7 @@ __device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const i
             const int o = __shfl_up_sync(0xffffffffu, incl, off);
             if (lane >= off) incl += o;
         }
-        if (lane == 31) sh->warp_tot[warp] = incl;
+        if (lane == 31 && act) sh->warp_tot[warp] = incl;
         __syncthreads();
         int pos = carry + incl - cnt, total = 0;
         for (int w = 0; w < kRowWarps; ++w) {
@@ -115,6 +108,55 @@ __device__ void ctc_collapse(int64_t u, int64_t n_frames, int32_t blank, const i
         __syncthreads();  // warp_tot is rewritten by the next pass
     }
     if (threadIdx.x == 0) out_len[u] = carry;
+}
+
+// After a CTA's frames [f_lo, f_hi) are all written: collapses the utterances it holds whole, and those
+// split across CTAs whose frame count it completes (a ticket per split utterance, at the CTA holding
+// its first frame; at most one split utterance starts in any CTA). `start(c)` gives CTA c's first frame.
+template <class Start>
+__device__ void ctc_finish_cta(int64_t f_lo, int64_t f_hi, int64_t n_utt, int64_t n_frames, int32_t blank,
+                               const int32_t* frame_ids, int32_t* out_ids, int32_t* out_frames, int32_t* out_len,
+                               int* tickets, CtcShared* sh, Start start) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        sh->n_last = 0;
+        const int64_t G = gridDim.x;
+        if (f_hi > f_lo) {
+            const int64_t u0 = f_lo / n_frames, u1 = (f_hi - 1) / n_frames;
+            for (int64_t u = u0; u <= u1; ++u) {
+                const int64_t a = u * n_frames > f_lo ? u * n_frames : f_lo;
+                const int64_t b = (u + 1) * n_frames < f_hi ? (u + 1) * n_frames : f_hi;
+                const int n = static_cast<int>(b - a);
+                if (n == n_frames) {
+                    sh->last_utt[sh->n_last] = u;
+                    sh->last_ticket[sh->n_last++] = -1;
+                    continue;
+                }
+                // the CTA holding the utterance's first frame
+                const int64_t f = u * n_frames;
+                int64_t c = f * G / (n_utt * n_frames);
+                if (c >= G) c = G - 1;
+                while (c + 1 < G && start(c + 1) <= f) ++c;
+                while (c > 0 && start(c) > f) --c;
+                const int t = static_cast<int>(c);
+                const int prev = atomicAdd(&tickets[t], n);
+                if (prev + n == n_frames) {
+                    sh->last_utt[sh->n_last] = u;
+                    sh->last_ticket[sh->n_last++] = t;
+                }
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    const int n_last = sh->n_last;
+    for (int j = 0; j < n_last; ++j) {
+        const int64_t u = sh->last_utt[j];
+        const int t = sh->last_ticket[j];
+        ctc_collapse(u, n_frames, blank, frame_ids, out_ids, out_frames, out_len, sh);
+        if (threadIdx.x == 0 && t >= 0) tickets[t] = 0;
+    }
 }
 
 template <int kDtype, bool kLogp>
@@ -146,43 +188,8 @@ __global__ void __launch_bounds__(kRowNT) ctc_kernel(const unsigned char* logits
             }
         }
     }
-    // Every frame of this CTA is written. An utterance held whole here is collapsed here; one split
-    // across CTAs counts its frames on the ticket of the CTA holding its first frame (at most one
-    // split utterance starts in any CTA), and whichever CTA completes the count collapses it.
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        sh.n_last = 0;
-        const int64_t G = gridDim.x;
-        if (f_hi > f_lo) {
-            const int64_t u0 = f_lo / n_frames, u1 = (f_hi - 1) / n_frames;
-            for (int64_t u = u0; u <= u1; ++u) {
-                const int64_t a = u * n_frames > f_lo ? u * n_frames : f_lo;
-                const int64_t b = (u + 1) * n_frames < f_hi ? (u + 1) * n_frames : f_hi;
-                const int n = static_cast<int>(b - a);
-                if (n == n_frames) {
-                    sh.last_utt[sh.n_last] = u;
-                    sh.last_ticket[sh.n_last++] = -1;
-                    continue;
-                }
-                const int t = static_cast<int>(ctc_cta_of_frame(u * n_frames, total, G));
-                const int prev = atomicAdd(&tickets[t], n);
-                if (prev + n == n_frames) {
-                    sh.last_utt[sh.n_last] = u;
-                    sh.last_ticket[sh.n_last++] = t;
-                }
-            }
-        }
-        __threadfence();
-    }
-    __syncthreads();
-    const int n_last = sh.n_last;
-    for (int j = 0; j < n_last; ++j) {
-        const int64_t u = sh.last_utt[j];
-        const int t = sh.last_ticket[j];
-        ctc_collapse(u, n_frames, blank, frame_ids, out_ids, out_frames, out_len, &sh);
-        if (threadIdx.x == 0 && t >= 0) tickets[t] = 0;
-    }
+    ctc_finish_cta(f_lo, f_hi, n_utt, n_frames, blank, frame_ids, out_ids, out_frames, out_len, tickets, &sh,
+                   [&](int64_t c) { return ctc_range_start(c, total, gridDim.x); });
 }
 
 }  // namespace
