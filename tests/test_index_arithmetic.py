@@ -143,3 +143,65 @@ def test_ctc_ranges_and_tickets(n_utt, n_frames):
             split_first[first] = u
     # a CTA collapses its whole utterances plus at most one split utterance it completes
     assert max(whole) <= CTC_MAX_UTT_PER_CTA - 2
+
+
+RING_FRAMES = 8           # select_ctc.cu: kRingFrames
+RING_MAX_STAGE = 36864    # kRingMaxStageBytes
+MAX_UTT_PER_CTA = 64      # kMaxUttPerCta
+
+
+def ring_eligible(n_utt, n_frames, n_classes, esz, sms=148):
+    G = 2 * sms
+    total = n_utt * n_frames
+    t8 = total - total % RING_FRAMES
+    max_range = (t8 + G - 1) // G + 2 * RING_FRAMES
+    return RING_FRAMES * n_classes * esz <= RING_MAX_STAGE and G <= TICKET_SLOTS and \
+        max_range <= (MAX_UTT_PER_CTA - 2) * n_frames
+
+
+def ring_start(c, t8, G, total):
+    if c >= G:
+        return total
+    p = c * t8 // G
+    return p - p % RING_FRAMES
+
+
+@pytest.mark.parametrize("n_utt,n_frames", list(itertools.product([1, 2, 5, 32, 100, 600, 4000],
+                                                                  [1, 3, 7, 8, 17, 100, 1500, 3000])))
+@pytest.mark.parametrize("n_classes,esz", [(1025, 4), (1025, 2), (51865 // 16, 4), (1, 4), (3, 2)])
+def test_ctc_ring_ranges_and_tickets(n_utt, n_frames, n_classes, esz):
+    """The ring CTC kernel (select_ctc.cu: ctc_ring_kernel, launch_ctc): every stage is one bulk copy of
+    eight whole frames starting on a 16-byte boundary, the ranges cover every frame once, and the
+    split-utterance tickets and the per-CTA collapse list stay within their bounds."""
+    if not ring_eligible(n_utt, n_frames, n_classes, esz):
+        return
+    G, total = 2 * 148, n_utt * n_frames
+    t8 = total - total % RING_FRAMES
+    row = n_classes * esz
+    assert (RING_FRAMES * row) % 16 == 0                    # each stage: a legal bulk-copy size
+    lo = [ring_start(c, t8, G, total) for c in range(G)]
+    ring_hi = [ring_start(c + 1, t8, G, total) if c + 1 < G else t8 for c in range(G)]
+    hi = [ring_hi[c] if c + 1 < G else total for c in range(G)]
+    assert lo[0] == 0 and hi[-1] == total
+    assert all(hi[c] == lo[c + 1] for c in range(G - 1))    # contiguous, no gap, no overlap
+    for c in range(G):
+        assert lo[c] <= ring_hi[c] <= hi[c]
+        assert lo[c] % RING_FRAMES == 0 and (ring_hi[c] - lo[c]) % RING_FRAMES == 0
+        assert (lo[c] * row) % 16 == 0                      # stage sources 16-byte aligned
+        assert hi[c] - ring_hi[c] < RING_FRAMES and (c == G - 1 or hi[c] == ring_hi[c])
+    split_first = {}
+    whole = [0] * G
+    for u in range(n_utt):
+        a, b = u * n_frames, (u + 1) * n_frames
+        holders = [c for c in range(G) if lo[c] < b and hi[c] > a]
+        assert holders == list(range(holders[0], holders[-1] + 1))
+        if len(holders) == 1:
+            whole[holders[0]] += 1
+        else:
+            first = holders[0]
+            assert first not in split_first, "two split utterances start in one CTA: ticket clash"
+            split_first[first] = u
+            assert first < TICKET_SLOTS
+    # a CTA collapses its whole utterances and at most the two split ones it touches (first, last):
+    # CtcShared.last_utt holds kMaxUttPerCta
+    assert max(whole) + 2 <= MAX_UTT_PER_CTA
