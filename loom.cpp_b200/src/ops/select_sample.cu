@@ -1045,6 +1045,8 @@ struct WarpSampleOp {
         tv = neg_inf();
         wv = neg_inf();
         pending = false;
+        // this thread's first history id is loaded before the set is cleared (its latency overlaps)
+        const int32_t id_first = tid < p.hist_len ? __ldg(row_hist(s.row) + tid) : 0;
         if (p.penalty) {
             int4* h4 = reinterpret_cast<int4*>(hset);
             for (int i = tid; i < kHashSlots / 4; i += kNT) h4[i] = make_int4(-1, -1, -1, -1);
@@ -1053,7 +1055,7 @@ struct WarpSampleOp {
         // validate the whole history; the distinct ids inside this segment go into the set and list
         const int64_t seg_lo = p.vocab_offset + s.j0, seg_hi = p.vocab_offset + s.j1;
         for (int j = tid; j < p.hist_len; j += kNT) {
-            const int32_t id = __ldg(row_hist(s.row) + j);
+            const int32_t id = j == tid ? id_first : __ldg(row_hist(s.row) + j);
             if (id < 0 || id >= p.vocab_limit) sh->bad = 1;
             else if (p.penalty && id >= seg_lo && id < seg_hi && hash_insert(hset, id))
                 uniq[atomicAdd(&sh->n_uniq, 1)] = id;
@@ -1216,6 +1218,12 @@ struct WarpSampleOp {
 
     __device__ void end_segment(const Segment& s) {
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        // the first of this lane's history logits, loaded before the prune (its latency overlaps)
+        const int nu0 = p.penalty ? sh->n_uniq : 0;
+        const int j_first = warp * 32 + lane;
+        float x_first = 0.0f;
+        if (j_first < nu0)
+            x_first = load_global_elem<kDtype>(row_ptr(s.row), static_cast<int64_t>(uniq[j_first]) - p.vocab_offset);
         prune();  // at most k keys per warp, the raw buffer empty
         if (kLse && ls > 0.0f) {
             // the streamed sum, relative to the tempered maximum: 2^((x - lm) c) = e^(x / T - lm / T)
@@ -1235,7 +1243,9 @@ struct WarpSampleOp {
                 bool keep = false;
                 if (j < nu) {
                     const int32_t id = uniq[j];
-                    const float x = load_global_elem<kDtype>(row_ptr(s.row), static_cast<int64_t>(id) - p.vocab_offset);
+                    const float x = j == j_first ? x_first
+                                                 : load_global_elem<kDtype>(row_ptr(s.row),
+                                                                            static_cast<int64_t>(id) - p.vocab_offset);
                     const float y = tempered(penalise(x, p.r), p.T, p.greedy);
                     if (p.lse) lse_offer(lse, y);
                     key = loom_rank_key(y, id);
