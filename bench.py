@@ -612,7 +612,7 @@ def run_ctc(args, sel, synth, torch, dev, rank, world, peak, cpu):
     gbs = U * F * C * 4 / (call_ms / 1e3) / 1e9
     res = {"config": "greedy CTC, [32, 1500, 1025] f32 N(0, 1) (+4 on the blank 1024 for 70% of frames, else on a "
                      "random id)", "ms_per_step": med, "frames_per_s": U * F * world / (med / 1e3),
-           "hbm_gbs": gbs, "hbm_frac": gbs / peak, "traffic": profiled_traffic("ctc_kernel_ctc"),
+           "hbm_gbs": gbs, "hbm_frac": gbs / peak, "traffic": profiled_traffic("ctc_ring_kernel_ctc"),
            "parity_ok": ok, "parity_against": "loom.cpp's own ctc_greedy_decode" if use_ref else "the oracle"}
     if cpu:
         got = np.zeros((U, F), dtype=np.int32)
