@@ -306,35 +306,15 @@ __global__ void __launch_bounds__(kRingThreads, 2)
             }
             waited = it + 1;
             const unsigned char* fr = ring + static_cast<size_t>(slot) * stage_bytes + warp * row_bytes;
-            // four independent (value, column) chains per lane (columns j, j + 32, j + 64, j + 96),
-            // merged with the same order-free rule
-            ArgBest best = arg_init(), b1 = arg_init(), b2 = arg_init(), b3 = arg_init();
+            ArgBest best = arg_init();
             LseAcc lse = lse_init();
-            const float x0 = smem_frame_elem<kDtype>(fr, 0);  // (lane 0's column 0; read by all, used by lane 0)
-            int32_t j = lane;
-            const int32_t C = static_cast<int32_t>(n_classes);
-            for (; j + 96 < C; j += 128) {
-                const float xa = smem_frame_elem<kDtype>(fr, j), xb = smem_frame_elem<kDtype>(fr, j + 32);
-                const float xc = smem_frame_elem<kDtype>(fr, j + 64), xd = smem_frame_elem<kDtype>(fr, j + 96);
-                arg_offer(best, xa, j);
-                arg_offer(b1, xb, j + 32);
-                arg_offer(b2, xc, j + 64);
-                arg_offer(b3, xd, j + 96);
-                if constexpr (kLogp) {
-                    lse_offer(lse, xa);
-                    lse_offer(lse, xb);
-                    lse_offer(lse, xc);
-                    lse_offer(lse, xd);
-                }
-            }
-            for (; j < C; j += 32) {
+            float x0 = 0.0f;
+            for (int64_t j = lane; j < n_classes; j += 32) {
                 const float x = smem_frame_elem<kDtype>(fr, j);
-                arg_offer(best, x, j);
+                if (j == 0) x0 = x;
+                arg_offer(best, x, static_cast<int32_t>(j));
                 if constexpr (kLogp) lse_offer(lse, x);
             }
-            arg_offer(best, b1.v, b1.i);
-            arg_offer(best, b2.v, b2.i);
-            arg_offer(best, b3.v, b3.i);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl.empty[slot]);
