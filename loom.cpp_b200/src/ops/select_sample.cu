@@ -96,7 +96,6 @@ struct SampleShared {
     uint32_t x_key;            // warp path: order key of the raw threshold X
     float wq[kSampWarps];      // warp path: per warp, a raw value that ceil(k / warps) of its lanes' maxima reach
     float u_row;               // the segment's row's uniform (loaded when the segment starts)
-    unsigned long long wkq[kSampWarps];  // warp path: per warp, its ceil(k / warps)-th kept key (0: none yet)
     int mcnt[32];              // split-row merge: the batch's piece counts (-1: a bad history id)
     LseAcc mpart[32];          // and their log-sum-exp states
 };
@@ -942,19 +941,6 @@ struct WarpSampleOp {
         if (kth > old) atomicMax(&sh->x_key, loom_order_key(inverse_threshold_bound(rank_key_value(kth), p.T, p.greedy)));
     }
 
-    // One lane: the warp keeps ceil(k / warps) keys that reach `key`; once every warp has published
-    // such a key, the smallest is reached by at least k distinct elements.
-    __device__ void publish_key(uint64_t key) {
-        volatile unsigned long long* wkq = sh->wkq;
-        wkq[threadIdx.x >> 5] = key;
-        unsigned long long mn = key;
-        for (int w = 0; w < kSampWarps; ++w) {
-            const unsigned long long o = wkq[w];
-            mn = o < mn ? o : mn;
-        }
-        if (mn != 0ull) raise(mn);
-    }
-
     // One lane: at least k distinct non-history elements have a raw value >= v.
     __device__ void raise_raw(float v) {
         const float t = tempered(v, p.T, p.greedy);
@@ -1021,16 +1007,9 @@ struct WarpSampleOp {
         }
         nr = 0;
         __syncwarp();
-        // with ceil(k / warps) keys, sort: the warp's ceil(k / warps)-th key is published (the smallest
-        // of the warps' published keys is reached by k distinct elements), and with k keys the k-th
-        // raises the thresholds directly
-        const int q = (p.k + kSampWarps - 1) / kSampWarps;
-        if (n >= q) {
+        if (n >= p.k) {
             n = warp_keep_best(wk, n, p.k);
-            if (lane == 0) {
-                publish_key(wk[q - 1]);
-                if (n >= p.k) raise(wk[p.k - 1]);
-            }
+            if (lane == 0) raise(wk[p.k - 1]);
         }
         nk = n;
     }
@@ -1054,7 +1033,6 @@ struct WarpSampleOp {
             sh->n_uniq = 0;
             sh->warm_key = 0xffffffffu;
             sh->key_t = 0ull;
-            for (int w = 0; w < kSampWarps; ++w) sh->wkq[w] = 0ull;
             sh->x_key = loom_order_key(neg_inf());
             for (int w = 0; w < kSampWarps; ++w) sh->wq[w] = neg_inf();
         }
