@@ -722,32 +722,6 @@ __device__ __forceinline__ uint64_t f32x2_splat(float v) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// a and b: 64 rank keys each, two per lane (element j * 32 + lane in slot j), sorted best first, 0
-// where empty. Leaves in a the 64 best keys of both, sorted best first: max(a_i, b_{63-i}) is a
-// bitonic sequence holding the 64 best, and a bitonic merge sorts it.
-__device__ __forceinline__ void merge_top64(uint64_t& a0, uint64_t& a1, uint64_t b0, uint64_t b1) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t r0 = __shfl_sync(0xffffffffu, b1, 31 - lane);
-    const uint64_t r1 = __shfl_sync(0xffffffffu, b0, 31 - lane);
-    uint64_t x0 = a0 > r0 ? a0 : r0;
-    uint64_t x1 = a1 > r1 ? a1 : r1;
-    {
-        const uint64_t hi = x0 > x1 ? x0 : x1, lo = x0 > x1 ? x1 : x0;
-        x0 = hi;
-        x1 = lo;
-    }
-#pragma unroll
-    for (int stride = 16; stride > 0; stride >>= 1) {
-        const uint64_t o0 = __shfl_xor_sync(0xffffffffu, x0, stride);
-        const uint64_t o1 = __shfl_xor_sync(0xffffffffu, x1, stride);
-        const bool lower = (lane & stride) == 0;
-        x0 = lower ? (x0 > o0 ? x0 : o0) : (x0 > o0 ? o0 : x0);
-        x1 = lower ? (x1 > o1 ? x1 : o1) : (x1 > o1 ? o1 : x1);
-    }
-    a0 = x0;
-    a1 = x1;
-}
-
 __device__ __forceinline__ uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
@@ -1289,44 +1263,18 @@ struct WarpSampleOp {
             if (lane == 0) sh->lse_w[warp] = w;
         }
         group_sync<kNT>();  // every raw buffer is empty: the gather (which aliases them) is free
+        int off = 0;
+        if (lane == 0) off = atomicAdd(&sh->K, nk);
+        off = __shfl_sync(0xffffffffu, off, 0);
+        for (int i = lane; i < nk; i += 32) cand[off + i] = wk[i];
         if (tid == 0) {
             LseAcc a = lse_init();
             if (p.lse)
                 for (int w = 0; w < kSampWarps; ++w) a = lse_merge(a, sh->lse_w[w]);
             sh->seg_lse = a;
         }
-        int K;
-        if (p.k <= 64) {
-            // each warp sorts its best keys; a merge tree of sorted 64-key lists (warp w + s hands its
-            // list to warp w through slot w + s of the gather) leaves the CTA's best 64 in warp 0
-            if (nk > 0) nk = warp_keep_best(wk, nk, p.k);
-            uint64_t a0 = lane < nk ? wk[lane] : 0ull, a1 = lane + 32 < nk ? wk[lane + 32] : 0ull;
-#pragma unroll
-            for (int step = 1; step < kSampWarps; step <<= 1) {
-                if ((warp & (2 * step - 1)) == step) {
-                    cand[warp * 64 + lane] = a0;
-                    cand[warp * 64 + 32 + lane] = a1;
-                }
-                group_sync<kNT>();
-                if ((warp & (2 * step - 1)) == 0)
-                    merge_top64(a0, a1, cand[(warp + step) * 64 + lane], cand[(warp + step) * 64 + 32 + lane]);
-            }
-            if (warp == 0) {
-                cand[lane] = a0;
-                cand[32 + lane] = a1;
-                int n = __popc(__ballot_sync(0xffffffffu, a0 != 0ull)) + __popc(__ballot_sync(0xffffffffu, a1 != 0ull));
-                if (lane == 0) sh->K = n < p.k ? n : p.k;
-            }
-            group_sync<kNT>();
-            K = sh->K;
-        } else {
-            int off = 0;
-            if (lane == 0) off = atomicAdd(&sh->K, nk);
-            off = __shfl_sync(0xffffffffu, off, 0);
-            for (int i = lane; i < nk; i += 32) cand[off + i] = wk[i];
-            group_sync<kNT>();
-            K = topk_select_sorted_small_k<kNT, kWarpCand>(cand, sh->K, p.k, &sh->tk);
-        }
+        group_sync<kNT>();
+        const int K = topk_select_sorted_small_k<kNT, kWarpCand>(cand, sh->K, p.k, &sh->tk);
         double* e = reinterpret_cast<double*>(keys0);
         finish_segment<kDtype, kNT, kWarpCand, true>(p, g, s, cand, e, e + kWarpMaxK, K, sh->seg_lse, sh->bad != 0, sh);
     }

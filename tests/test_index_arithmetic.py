@@ -205,47 +205,3 @@ def test_ctc_ring_ranges_and_tickets(n_utt, n_frames, n_classes, esz):
     # a CTA collapses its whole utterances and at most the two split ones it touches (first, last):
     # CtcShared.last_utt holds kMaxUttPerCta
     assert max(whole) + 2 <= MAX_UTT_PER_CTA
-
-
-def merge_top64(a, b):
-    """Lane-by-lane restatement of merge_top64 in select_sample.cu: a and b are 64 keys each,
-    element j * 32 + lane in slot j of lane `lane`, sorted best first (0 = empty)."""
-    x = [max(a[i], b[63 - i]) for i in range(64)]
-    for i in range(32):  # the in-lane stride-32 step
-        x[i], x[i + 32] = max(x[i], x[i + 32]), min(x[i], x[i + 32])
-    for stride in (16, 8, 4, 2, 1):  # shuffles within each 32-element half
-        y = list(x)
-        for i in range(64):
-            lane, o = i & 31, i ^ stride
-            y[i] = max(x[i], x[o]) if (lane & stride) == 0 else min(x[i], x[o])
-        x = y
-    return x
-
-
-def cta_merge_tree(lists, warps=8):
-    """The segment-end merge tree for top_k <= 64: warp w + step hands its sorted list to warp w."""
-    regs = [sorted(l, reverse=True) + [0] * (64 - len(l)) for l in lists]
-    step = 1
-    while step < warps:
-        for w in range(0, warps, 2 * step):
-            regs[w] = merge_top64(regs[w], regs[w + step])
-        step *= 2
-    return regs[0]
-
-
-@pytest.mark.parametrize("seed", range(40))
-def test_merge_tree_keeps_the_best_sorted(seed):
-    import random
-
-    rng = random.Random(seed)
-    k = rng.choice([1, 2, 7, 32, 40, 63, 64])
-    keys = rng.sample(range(1, 1 << 40), 8 * 64)
-    lists = []
-    for w in range(8):
-        n = rng.choice([0, 1, k // 2, k]) if seed % 3 else k
-        lists.append(sorted(keys[w * 64:w * 64 + n], reverse=True)[:k])
-    got = cta_merge_tree(lists)
-    want = sorted((x for l in lists for x in l), reverse=True)
-    n = min(len(want), k)
-    assert got[:n] == want[:n]
-    assert sum(1 for x in got if x) == min(len(want), 64)
