@@ -647,6 +647,60 @@ def run_ctc(args, sel, synth, torch, dev, rank, world, peak, cpu):
     return res
 
 
+def run_lm_head(args, sel, torch, dev, rank, world, peak):
+    """Greedy selection fused into the LM-head GEMM (loom_lm_head_argmax) against the unfused path the
+    engine runs today: a library GEMM writing bf16 logits, then loom_argmax_rows reading them back.
+    [rows, 2048] bf16 hidden states x a [151936, 2048] bf16 weight (a Qwen-size LM head, 622 MB; two
+    copies alternate, so the weight is never L2-resident). Tensor-bound at 1024 rows, HBM-bound at 1."""
+    hdim, tol = 2048, 2e-3
+    g = torch.Generator(device=dev).manual_seed(17 + rank)
+    weights = [(torch.randn(VOCAB, hdim, generator=g, device=dev) * (1.0 / hdim ** 0.5)).to(torch.bfloat16)
+               for _ in range(2)]
+    ws = sel.Workspace(dev)
+    out = {"config": f"hidden [rows, {hdim}] bf16 x lm_head [{VOCAB}, {hdim}] bf16 (two alternating copies), "
+                     "greedy id + logit + log-sum-exp per row",
+           "tensor_peak_tflops": 1590.0, "tensor_peak_source": "fallback (no measured bf16 figure here)"}
+    for rows in (1, ROWS):
+        hidden = torch.randn(rows, hdim, generator=g, device=dev).to(torch.bfloat16)
+        ids = torch.empty(rows, dtype=torch.int32, device=dev)
+        logit = torch.empty(rows, dtype=torch.float32, device=dev)
+        lse = torch.empty(rows, dtype=torch.float32, device=dev)
+        ids_u = torch.empty(rows, dtype=torch.int32, device=dev)
+
+        def fused(i):
+            sel.lm_head_argmax_into(hidden, weights[i & 1], ids, logit, lse, workspace=ws)
+
+        def unfused(i):
+            sel.argmax_rows_into(hidden @ weights[i & 1].t(), ids_u, workspace=ws)
+
+        res = {}
+        for name, fn in (("fused", fused), ("unfused_gemm_then_argmax", unfused)):
+            for i in range(3):
+                fn(i)
+            steps = max(args.steps, 20)
+            regions, call_ms = timed_regions(fn, steps, world, args.extra_seconds / 4)
+            res[name + "_us"] = 1e3 * statistics.median(regions) / steps
+        fused(0)
+        torch.cuda.synchronize()
+        ref = hidden.float() @ weights[0].float().t()
+        chosen = ref.gather(1, ids.long()[:, None])[:, 0]
+        ok = bool((chosen >= ref.max(dim=1).values - tol).all()) and \
+            bool(torch.allclose(lse, torch.logsumexp(ref, dim=1), atol=tol, rtol=0)) and \
+            ws.read_status() == sel.OK
+        del ref
+        us = res["fused_us"]
+        flops = 2.0 * rows * hdim * VOCAB
+        res.update({"rows_per_s": rows * world / (us / 1e6), "tflops": flops / (us / 1e6) / 1e12,
+                    "weight_gbs": VOCAB * hdim * 2 / (us / 1e6) / 1e9,
+                    "speedup_vs_unfused": res["unfused_gemm_then_argmax_us"] / us,
+                    "parity_ok": all_true(ok, world)})
+        res["tensor_frac"] = res["tflops"] / out["tensor_peak_tflops"]
+        res["hbm_frac"] = res["weight_gbs"] / peak
+        out[f"rows_{rows}"] = res
+    del weights
+    return out
+
+
 def cpu_baseline_sample(synth, rows=1024, min_seconds=10.0):
     """The oracle's sampling chain on the [rows, V] host batch with all host threads, repeated until at
     least `min_seconds` have passed (a bounded sample). Returns (rows/s, seconds, passes, threads)."""
@@ -752,6 +806,8 @@ def run_b200(args):
         extras["greedy"] = run_greedy(args, sel, synth, torch, dev, rank, world, peak, cpu)
     if only in (None, "ctc"):
         extras["ctc"] = run_ctc(args, sel, synth, torch, dev, rank, world, peak, cpu)
+    if only in (None, "lm_head"):
+        extras["lm_head"] = run_lm_head(args, sel, torch, dev, rank, world, peak)
     line.update(extras)
     if "sweep" in extras:
         strong = [s for s in extras["sweep"] if s["global_batch"] == ROWS][0]
@@ -780,7 +836,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default=None, choices=["sample", "sweep", "shard", "decode", "greedy", "ctc"],
+    ap.add_argument("--workload", default=None, choices=["sample", "sweep", "shard", "decode", "greedy", "ctc", "lm_head"],
                     help="run one workload alone (profiling)")
     ap.add_argument("--min-seconds", type=float, default=1.0, help="device time of the headline's timed regions")
     ap.add_argument("--extra-seconds", type=float, default=0.25, help="device time of each other workload")

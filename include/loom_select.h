@@ -246,6 +246,23 @@ LOOM_SELECT_API int loom_ctc_greedy(const void* logits, int dtype, int64_t n_utt
                     int32_t* out_frame_ids, float* out_frame_logp, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/*
+ * Greedy selection fused into the LM-head GEMM: logits[r, v] = sum_h hidden[r, h] * weight[v, h]
+ * (bf16 inputs, f32 tensor-core accumulation) are reduced tile by tile on chip and never written to
+ * memory. Replaces ggml's mul_mat(lm_head, hidden) that ends loom.cpp's text models followed by
+ * Generator::argmax (src/core/generation.cpp:64-74); the weight layout is ggml's: [n_vocab,
+ * hidden_dim] row-major. out_ids[r] follows the loom_argmax_rows rule on those f32 logits (lowest id
+ * among equal maxima, a NaN at id 0 wins, a NaN elsewhere never wins); out_logit[r] (NULL to skip) is
+ * the winning logit and out_lse[r] (NULL to skip) the row's log-sum-exp, so out_logit - out_lse is
+ * the greedy token's log-probability. Requirements: hidden_dim a multiple of 64 (LOOM_SELECT_ESHAPE
+ * otherwise), hidden and weight 16-byte aligned with rows packed (row stride = hidden_dim). Device
+ * errors (a bounded wait that gave up) are read with loom_select_read_status.
+ */
+LOOM_SELECT_API size_t loom_lm_head_workspace_size(int64_t rows, int64_t n_vocab);
+LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, int64_t rows, int64_t hidden_dim,
+                                        int64_t n_vocab, int32_t* out_ids, float* out_logit, float* out_lse,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -25,7 +25,8 @@ SOURCES = [("select_capi.cu", "select_capi.o", []),
            ("select_ctc.cu", "select_ctc.o", []),
            ("select_sample.cu", "select_sample.o", []),
            ("select_noalloc.cu", "select_noalloc.o", []),
-           ("select_windows.cu", "select_windows.o", [])]
+           ("select_windows.cu", "select_windows.o", []),
+           ("select_lmhead.cu", "select_lmhead.o", [])]
 
 # sm_100a only. --fmad=false: no multiply-add contraction anywhere, so every float expression
 # rounds as written (the decision arithmetic also spells its operations as explicit intrinsics).

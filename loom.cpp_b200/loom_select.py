@@ -58,6 +58,8 @@ EXPORTS = (
     "loom_sample_shard_partial",
     "loom_sample_shard_merge",
     "loom_ctc_greedy",
+    "loom_lm_head_workspace_size",
+    "loom_lm_head_argmax",
 )
 
 
@@ -109,6 +111,8 @@ def _lib():
             "loom_sample_shard_merge": (ctypes.c_int, [vp, i32, i64, vp, ctypes.POINTER(SampleParams),
                                                        vp, vp, vp, vp, vp]),
             "loom_ctc_greedy": (ctypes.c_int, [vp, ctypes.c_int, i64, i64, i64, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
+            "loom_lm_head_workspace_size": (sz, [i64, i64]),
+            "loom_lm_head_argmax": (ctypes.c_int, [vp, vp, i64, i64, i64, vp, vp, vp, vp, sz, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(lib, name)
@@ -385,3 +389,43 @@ def ctc_greedy_decode(logits, blank_id, workspace=None, stream=None):
     ids, _, lens = ctc_greedy(logits, blank_id, workspace=workspace, stream=stream)
     n = int(lens[0].item())
     return ids[0, :n].cpu().tolist()
+
+
+# ----------------------------------------------------------------------------------------------
+# greedy selection fused into the LM-head GEMM
+
+def lm_head_argmax_into(hidden, weight, out_ids, out_logit=None, out_lse=None, workspace=None, stream=None):
+    """Greedy ids of logits = hidden @ weight.T without materialising the logits (asynchronous).
+
+    hidden [rows, hidden_dim] and weight [n_vocab, hidden_dim] are contiguous bf16 CUDA tensors (the
+    weight in ggml's lm_head layout); out_ids int32 [rows]; out_logit / out_lse f32 [rows] or None."""
+    torch = _torch()
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise SelectError(EDTYPE, "lm_head_argmax takes bf16 hidden states and weight")
+    if hidden.dim() == 1:
+        hidden = hidden.view(1, -1)
+    if hidden.dim() != 2 or weight.dim() != 2 or not hidden.is_contiguous() or not weight.is_contiguous():
+        raise SelectError(EINVAL, "hidden [rows, hidden_dim] and weight [n_vocab, hidden_dim] must be contiguous")
+    if hidden.shape[1] != weight.shape[1]:
+        raise SelectError(EINVAL, "hidden and weight disagree on hidden_dim")
+    rows, hdim = hidden.shape
+    n_vocab = weight.shape[0]
+    ws = workspace or default_workspace()
+    need = _lib().loom_lm_head_workspace_size(rows, n_vocab)
+    buf = ws.get(need, stream)
+    check(_lib().loom_lm_head_argmax(_ptr(hidden), _ptr(weight), rows, hdim, n_vocab, _ptr(out_ids),
+                                     _ptr(out_logit), _ptr(out_lse), _ptr(buf), buf.numel(), _stream_handle(stream)),
+          "loom_lm_head_argmax")
+    return out_ids
+
+
+def lm_head_argmax(hidden, weight, want_logit=True, want_lse=True, workspace=None, stream=None):
+    """(ids, logit or None, log-sum-exp or None) per row of hidden @ weight.T."""
+    torch = _torch()
+    rows = 1 if hidden.dim() == 1 else hidden.shape[0]
+    dev = hidden.device
+    ids = torch.empty(rows, dtype=torch.int32, device=dev)
+    logit = torch.empty(rows, dtype=torch.float32, device=dev) if want_logit else None
+    lse = torch.empty(rows, dtype=torch.float32, device=dev) if want_lse else None
+    lm_head_argmax_into(hidden, weight, ids, logit, lse, workspace, stream)
+    return ids, logit, lse

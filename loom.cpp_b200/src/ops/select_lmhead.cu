@@ -1,0 +1,461 @@
+// select_lmhead.cu -- greedy selection fused into the LM-head GEMM (sm_100a: TMA + tcgen05 + TMEM).
+//
+// loom.cpp's text models end in ggml's mul_mat(lm_head, hidden): logits[r, v] = sum_h hidden[r, h] *
+// weight[v, h], with the weight stored [n_vocab, hidden_dim] row-major (ggml ne0 = hidden_dim). The
+// engine then writes the [rows, n_vocab] logits to memory and Generator::argmax
+// (src/core/generation.cpp:64-74) scans them. Here the product is computed tile by tile on the
+// tensor cores and reduced before it ever leaves the SM:
+//
+//   * one persistent CTA per SM walks 128-row x 256-id tiles (row tile fastest, so the CTAs running
+//     at the same time share one weight tile through L2 and the weight is read from HBM about once);
+//   * warp 0 streams 64-wide K slices of the hidden and weight tiles into a 4-stage shared-memory
+//     ring with TMA (128-byte swizzle); warp 1 issues tcgen05.mma (M 128, N 256, K 16, bf16 in,
+//     f32 accumulate) into one of two 256-column TMEM accumulators;
+//   * warps 2-5 drain the other accumulator meanwhile (tcgen05.ld, one row per thread) and reduce each
+//     row's 256 logits to a record: the tile's maximum, the lowest id reaching it, the sum of
+//     exp(logit - maximum) when the log-sum-exp is wanted, and whether column 0 is NaN;
+//   * lm_merge_kernel folds a row's records (ascending id order) into the greedy id, its logit and
+//     the row's log-sum-exp.
+//
+// Selection rule (generation.cpp:64-74, a strict '>' scan from id 0): the lowest id among equal
+// maxima wins, a NaN at id 0 wins, a NaN anywhere else never wins. The logits themselves are f32 sums
+// of exact bf16 products in the tensor cores' order, so they can differ from another GEMM's in the
+// last bits; the id is the exact argmax of the logits this kernel computes.
+//
+// Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records LOOM_SELECT_ETIMEOUT in
+// the workspace, raises the CTA's abort flag, and every role winds down: the producer waits (again
+// bounded) for the copies it issued, the MMA warp for the MMAs it issued, then TMEM is freed.
+#include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "loom_select.h"
+#include "select_device.cuh"
+#include "select_internal.h"
+
+namespace loom_select {
+namespace {
+
+constexpr int kBM = 128;          // rows per tile (MMA M)
+constexpr int kBN = 256;          // ids per tile (MMA N)
+constexpr int kBK = 64;           // K slice per stage: 64 bf16 = 128 bytes, one swizzle span
+constexpr int kUK = 16;           // K per tcgen05.mma (kind::f16)
+constexpr int kStages = 4;
+constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
+constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KiB
+constexpr uint32_t kTileBBytes = kBN * kBK * 2;  // 32 KiB
+constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+constexpr uint32_t kTmemCols = 2 * kBN;          // two accumulators
+constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 256 + 1024;  // ring + barriers + 1 KiB alignment
+
+struct LmBars {
+    uint64_t full[kStages];    // TMA -> MMA
+    uint64_t empty[kStages];   // MMA -> TMA
+    uint64_t tfull[2];         // MMA -> epilogue
+    uint64_t tempty[2];        // epilogue -> MMA (4 arrivals: one per epilogue warp)
+    uint64_t drain;            // the MMA warp's final commit
+    uint32_t tmem_base;
+    int abort;
+};
+
+// ---- tcgen05 / TMA wrappers ----
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the 128-byte swizzle: rows of
+// 128 bytes, groups of 8 rows 1024 bytes apart (stride byte offset), descriptor version 1, layout
+// type 2 (128-byte swizzle). Stepping K by 16 elements inside the span adds 32 bytes to the start.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3FFF);
+    d |= uint64_t(1) << 16;                    // leading byte offset (unused for swizzled K-major)
+    d |= uint64_t((1024 >> 4) & 0x3FFF) << 32; // stride byte offset
+    d |= uint64_t(1) << 46;                    // version
+    d |= uint64_t(2) << 61;                    // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, N >> 3, M >> 4.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Bounded wait that also gives up as soon as another role of the CTA has aborted.
+__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_status(status, LOOM_SELECT_ETIMEOUT);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+struct LmArgs {
+    int64_t rows, n_vocab;
+    int k_blocks;          // hidden_dim / kBK
+    int m_tiles, v_tiles;  // tiles along rows and ids
+    float4* records;       // [v_tiles][rows]: (max, id bits, sum of exp, col-0 NaN flag)
+    int* status;
+    int want_lse;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    lm_head_argmax_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
+                          const LmArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    LmBars* bars = reinterpret_cast<LmBars*>(smem + size_t(kStages) * kStageBytes);
+    volatile int* abort_flag = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = a.m_tiles * a.v_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->tfull[b], 1);
+            mbar_init(&bars->tempty[b], 4);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars->tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- producer: TMA into the ring ----
+            int64_t kc = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const int mt = t % a.m_tiles, vt = t / a.m_tiles;
+                for (int kb = 0; kb < a.k_blocks; ++kb, ++kc) {
+                    const int s = int(kc % kStages);
+                    const int64_t n = kc / kStages;
+                    if (n >= 1 && !lm_wait(&bars->empty[s], uint32_t((n - 1) & 1), a.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = smem + size_t(s) * kStageBytes;
+                    mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+                    tma_load_2d(st, &map_h, kb * kBK, mt * kBM, &bars->full[s]);
+                    tma_load_2d(st + kTileABytes, &map_w, kb * kBK, vt * kBN, &bars->full[s]);
+                }
+            }
+            // Every copy issued lands before the CTA may exit (on the normal path the MMA warp has
+            // consumed them all already and these waits return at once).
+            for (int s = 0; s < kStages; ++s) {
+                if (kc > s) {
+                    const int64_t last = (kc - 1 - s) / kStages;
+                    mbar_wait_bounded(&bars->full[s], uint32_t(last & 1), a.status);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            int64_t kc = 0;
+            int i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++i) {
+                const int b = i & 1, u = i >> 1;
+                if (u >= 1 && !lm_wait(&bars->tempty[b], uint32_t((u - 1) & 1), a.status, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
+                for (int kb = 0; kb < a.k_blocks; ++kb, ++kc) {
+                    const int s = int(kc % kStages);
+                    const int64_t n = kc / kStages;
+                    if (!lm_wait(&bars->full[s], uint32_t(n & 1), a.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(smem + size_t(s) * kStageBytes);
+                    const uint32_t sb = sa + kTileABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / kUK; ++kk) {
+                        tc_mma(d_tmem, smem_desc_sw128(sa + kk * kUK * 2), smem_desc_sw128(sb + kk * kUK * 2),
+                               (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(&bars->empty[s]);
+                }
+                if (ok) tc_commit(&bars->tfull[b]);
+            }
+            // All MMAs issued have completed before TMEM is freed.
+            tc_commit(&bars->drain);
+            mbar_wait_bounded(&bars->drain, 0, a.status);
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue: warps 2-5 read TMEM lanes 32 * (warp % 4) .. + 31, one row per thread ----
+        const int q = warp & 3;
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            const int mt = t % a.m_tiles, vt = t / a.m_tiles;
+            const int b = i & 1, u = i >> 1;
+            const bool ok = lm_wait(&bars->tfull[b], uint32_t(u & 1), a.status, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * kBN);
+            const int64_t col0 = int64_t(vt) * kBN;
+            const int valid = a.n_vocab - col0 < kBN ? int(a.n_vocab - col0) : kBN;
+            float bv = -INFINITY;
+            int bi = -1;
+            float nan0 = 0.0f;
+            float v[32];
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                tc_ld32(taddr + uint32_t(c * 32), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int col = c * 32 + j;
+                    const float x = v[j];
+                    if (col < valid && (x > bv || (bi < 0 && x == x))) {
+                        bv = x;
+                        bi = col;
+                    }
+                }
+                if (c == 0 && vt == 0 && v[0] != v[0]) nan0 = 1.0f;
+            }
+            float sum = 0.0f;
+            if (a.want_lse) {
+                // Every lane makes the same tcgen05.ld calls (they are warp-collective); a lane whose
+                // tile part is all NaN sums against 0 and discards the result.
+                const float l2e = 1.4426950408889634f;
+                const float mb = bi >= 0 ? bv * l2e : 0.0f;
+                float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    tc_ld32(taddr + uint32_t(c * 32), v);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const int col = c * 32 + j;
+                        if (col < valid) s0 += fast_exp2(__fsub_rn(__fmul_rn(v[j], l2e), mb));
+                        if (col + 1 < valid) s1 += fast_exp2(__fsub_rn(__fmul_rn(v[j + 1], l2e), mb));
+                    }
+                }
+                sum = bi >= 0 ? s0 + s1 : 0.0f;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->tempty[b]);
+            const int64_t r = int64_t(mt) * kBM + q * 32 + lane;
+            if (r < a.rows) {
+                a.records[int64_t(vt) * a.rows + r] =
+                    make_float4(bv, __int_as_float(bi < 0 ? -1 : int(col0) + bi), sum, nan0);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// One warp per row: the row's records in ascending id order fold into (id, logit, log-sum-exp).
+__global__ void __launch_bounds__(256) lm_merge_kernel(const float4* __restrict__ records, int64_t rows, int v_tiles,
+                                                       int want_lse, int32_t* __restrict__ out_ids,
+                                                       float* __restrict__ out_logit, float* __restrict__ out_lse) {
+    const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int t = lane; t < v_tiles; t += 32) {
+        const float4 rec = records[int64_t(t) * rows + r];
+        const int id = __float_as_int(rec.y);
+        if (id >= 0 && (bi < 0 || rec.x > bv)) {  // ascending tiles: strict '>' keeps the lowest id
+            bv = rec.x;
+            bi = id;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const float4 first = records[r];  // tile 0 carries the column-0 NaN flag
+    const bool nan0 = first.w != 0.0f;
+    float lse = 0.0f;
+    if (want_lse) {
+        float s = 0.0f;
+        if (bi >= 0) {
+            for (int t = lane; t < v_tiles; t += 32) {
+                const float4 rec = records[int64_t(t) * rows + r];
+                if (__float_as_int(rec.y) >= 0 && rec.x != -INFINITY) s += rec.z * expf(rec.x - bv);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        lse = (bi >= 0 && !nan0) ? bv + logf(s) : __int_as_float(0x7fc00000);
+    }
+    if (lane == 0) {
+        const bool zero = nan0 || bi < 0;  // a NaN at id 0 (or only NaNs) leaves the scan at id 0
+        out_ids[r] = zero ? 0 : bi;
+        if (out_logit) out_logit[r] = zero ? __int_as_float(0x7fc00000) : bv;
+        if (out_lse) out_lse[r] = lse;
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {uint32_t(kBK), box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t v_tiles_of(int64_t n_vocab) { return (n_vocab + kBN - 1) / kBN; }
+
+}  // namespace
+}  // namespace loom_select
+
+using namespace loom_select;
+
+extern "C" {
+
+LOOM_SELECT_API size_t loom_lm_head_workspace_size(int64_t rows, int64_t n_vocab) {
+    if (rows <= 0 || n_vocab <= 0) return 0;
+    return ws_layout(sizeof(float4), rows * v_tiles_of(n_vocab)).bytes;
+}
+
+LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, int64_t rows, int64_t hidden_dim,
+                                        int64_t n_vocab, int32_t* out_ids, float* out_logit, float* out_lse,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+    if (!hidden || !weight || !out_ids) return LOOM_SELECT_EINVAL;
+    if (rows <= 0 || hidden_dim <= 0 || n_vocab <= 0) return LOOM_SELECT_EINVAL;
+    if (hidden_dim % kBK != 0 || rows > (int64_t(1) << 31) - 1 || n_vocab > (int64_t(1) << 31) - 1 ||
+        hidden_dim > (int64_t(1) << 20))
+        return LOOM_SELECT_ESHAPE;
+    if (reinterpret_cast<uintptr_t>(hidden) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
+        return LOOM_SELECT_EINVAL;
+    const int64_t vt = v_tiles_of(n_vocab), mt = (rows + kBM - 1) / kBM;
+    if (mt * vt > (int64_t(1) << 31) - 1) return LOOM_SELECT_ESHAPE;
+    const WsLayout l = ws_layout(sizeof(float4), rows * vt);
+    if (!workspace || workspace_bytes < l.bytes || reinterpret_cast<uintptr_t>(workspace) % kWsAlign != 0)
+        return LOOM_SELECT_EWORKSPACE;
+    int st = LOOM_SELECT_OK;
+    const int sms = device_sm_count(&st);
+    if (st != LOOM_SELECT_OK) return st;
+
+    CUtensorMap map_h, map_w;
+    if (!make_map(&map_h, hidden, uint64_t(hidden_dim), uint64_t(rows), kBM) ||
+        !make_map(&map_w, weight, uint64_t(hidden_dim), uint64_t(n_vocab), kBN))
+        return LOOM_SELECT_ECUDA;
+
+    static std::once_flag attr_once[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LOOM_SELECT_ECUDA;
+    cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once[dev], [&] {
+        attr_err = cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(kSmemBytes));
+    });
+    if (attr_err != cudaSuccess) return LOOM_SELECT_ECUDA;
+
+    LmArgs a;
+    a.rows = rows;
+    a.n_vocab = n_vocab;
+    a.k_blocks = int(hidden_dim / kBK);
+    a.m_tiles = int(mt);
+    a.v_tiles = int(vt);
+    a.records = reinterpret_cast<float4*>(static_cast<char*>(workspace) + l.records);
+    a.status = static_cast<int*>(workspace);
+    a.want_lse = out_lse != nullptr;
+    const int64_t tiles = mt * vt;
+    const int grid = int(tiles < sms ? tiles : sms);
+    auto s = static_cast<cudaStream_t>(stream);
+    lm_head_argmax_kernel<<<grid, kThreads, kSmemBytes, s>>>(map_h, map_w, a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return LOOM_SELECT_ECUDA;
+    lm_merge_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids,
+                                                              out_logit, out_lse);
+    return cudaGetLastError() == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA;
+}
+
+}  // extern "C"

@@ -106,6 +106,17 @@ def test_ctc_argument_checks():
     assert lib.loom_ctc_greedy(FAKE, 0, 1, 10, 4, 3, FAKE, FAKE, FAKE, None, None, FAKE, 64, None) == ls.EWORKSPACE
 
 
+def test_lm_head_argument_checks():
+    lib = ls.lib()
+    # hidden_dim not a multiple of 64, then null pointers, then a workspace that is too small
+    assert lib.loom_lm_head_argmax(FAKE, FAKE, 4, 100, 1000, FAKE, None, None, FAKE, 1 << 30, None) == ls.ESHAPE
+    assert lib.loom_lm_head_argmax(None, FAKE, 4, 128, 1000, FAKE, None, None, FAKE, 1 << 30, None) == ls.EINVAL
+    assert lib.loom_lm_head_argmax(FAKE, FAKE, 0, 128, 1000, FAKE, None, None, FAKE, 1 << 30, None) == ls.EINVAL
+    assert lib.loom_lm_head_argmax(FAKE, FAKE, 4, 128, 1000, FAKE, None, None, FAKE, 64, None) == ls.EWORKSPACE
+    need = lib.loom_lm_head_workspace_size(4, 1000)
+    assert need % 256 == 0 and need >= 256 + 4 * 4 * 16
+
+
 def test_python_mirror_raises_select_error():
     with pytest.raises(ls.SelectError) as e:
         ls.check(ls.EWINDOW, "loom.argmax_row_range")
