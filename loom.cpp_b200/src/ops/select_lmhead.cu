@@ -39,17 +39,30 @@ namespace loom_select {
 namespace {
 
 constexpr int kBM = 128;          // rows per tile (MMA M)
-constexpr int kBN = 256;          // ids per tile (MMA N)
 constexpr int kBK = 64;           // K slice per stage: 64 bf16 = 128 bytes, one swizzle span
 constexpr int kUK = 16;           // K per tcgen05.mma (kind::f16)
-constexpr int kStages = 4;
 constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KiB
-constexpr uint32_t kTileBBytes = kBN * kBK * 2;  // 32 KiB
-constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
-constexpr uint32_t kTmemCols = 2 * kBN;          // two accumulators
-constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 256 + 1024;  // ring + barriers + 1 KiB alignment
+constexpr uint32_t kTmemCols = 512;              // two accumulators, 256 columns apart
+constexpr int kAccStride = 256;
 
+// A tile is kBM rows x BN ids; the ring holds as many K slices as fit in shared memory. BN is a
+// multiple of 16 (an MMA N for M = 128) and keeps every stage a multiple of 1024 bytes (the 128-byte
+// swizzle's repeat).
+template <int BN>
+struct LmTile {
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tile width");
+    static constexpr uint32_t kTileBBytes = uint32_t(BN) * kBK * 2;
+    static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+    static_assert(kStageBytes % 1024 == 0, "stage alignment");
+    static constexpr int kStages = int((227u * 1024u - 2048u) / kStageBytes) < 6 ? int((227u * 1024u - 2048u) / kStageBytes) : 6;
+    static constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 256 + 1024;  // ring + barriers + alignment
+    // Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, N >> 3, M >> 4.
+    static constexpr uint32_t kIdesc =
+        (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+};
+
+template <int kStages>
 struct LmBars {
     uint64_t full[kStages];    // TMA -> MMA
     uint64_t empty[kStages];   // MMA -> TMA
@@ -86,13 +99,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, N >> 3, M >> 4.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -116,10 +127,55 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+template <int W>
+__device__ __forceinline__ void tc_ld(uint32_t taddr, float (&v)[W]) {
+    if constexpr (W == 32) tc_ld32(taddr, v);
+    else tc_ld16(taddr, v);
+}
+
+// The running (maximum, lowest id) of one row over W logits at tile columns [c0, c0 + W).
+template <int W>
+__device__ __forceinline__ void scan_chunk(const float (&v)[W], int c0, int valid, float& bv, int& bi) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        const int col = c0 + j;
+        const float x = v[j];
+        if (col < valid && (x > bv || (bi < 0 && x == x))) {
+            bv = x;
+            bi = col;
+        }
+    }
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Sum of 2^(v * log2(e) - mb) over the valid columns, two accumulators.
+template <int W>
+__device__ __forceinline__ void sum_chunk(const float (&v)[W], int c0, int valid, float mb, float& s0, float& s1) {
+    const float l2e = 1.4426950408889634f;
+#pragma unroll
+    for (int j = 0; j < W; j += 2) {
+        const int col = c0 + j;
+        if (col < valid) s0 += fast_exp2(__fsub_rn(__fmul_rn(v[j], l2e), mb));
+        if (col + 1 < valid) s1 += fast_exp2(__fsub_rn(__fmul_rn(v[j + 1], l2e), mb));
+    }
 }
 
 // Bounded wait that also gives up as soon as another role of the CTA has aborted.
@@ -146,12 +202,16 @@ struct LmArgs {
     int want_lse;
 };
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     lm_head_argmax_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                           const LmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    LmBars* bars = reinterpret_cast<LmBars*>(smem + size_t(kStages) * kStageBytes);
+    using T = LmTile<BN>;
+    constexpr int kStages = T::kStages;
+    constexpr uint32_t kStageBytes = T::kStageBytes;
+    LmBars<kStages>* bars = reinterpret_cast<LmBars<kStages>*>(smem + size_t(kStages) * kStageBytes);
     volatile int* abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -198,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     unsigned char* st = smem + size_t(s) * kStageBytes;
                     mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
                     tma_load_2d(st, &map_h, kb * kBK, mt * kBM, &bars->full[s]);
-                    tma_load_2d(st + kTileABytes, &map_w, kb * kBK, vt * kBN, &bars->full[s]);
+                    tma_load_2d(st + kTileABytes, &map_w, kb * kBK, vt * BN, &bars->full[s]);
                 }
             }
             // Every copy issued lands before the CTA may exit (on the normal path the MMA warp has
@@ -221,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int b = i & 1, u = i >> 1;
                 if (u >= 1 && !lm_wait(&bars->tempty[b], uint32_t((u - 1) & 1), a.status, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
+                const uint32_t d_tmem = tmem_base + uint32_t(b * kAccStride);
                 for (int kb = 0; kb < a.k_blocks; ++kb, ++kc) {
                     const int s = int(kc % kStages);
                     const int64_t n = kc / kStages;
@@ -235,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / kUK; ++kk) {
                         tc_mma(d_tmem, smem_desc_sw128(sa + kk * kUK * 2), smem_desc_sw128(sb + kk * kUK * 2),
-                               (kb | kk) != 0 ? 1u : 0u);
+                               T::kIdesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     tc_commit(&bars->empty[s]);
                 }
@@ -256,43 +316,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool ok = lm_wait(&bars->tfull[b], uint32_t(u & 1), a.status, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * kBN);
-            const int64_t col0 = int64_t(vt) * kBN;
-            const int valid = a.n_vocab - col0 < kBN ? int(a.n_vocab - col0) : kBN;
+            const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * kAccStride);
+            const int64_t col0 = int64_t(vt) * BN;
+            const int valid = a.n_vocab - col0 < BN ? int(a.n_vocab - col0) : BN;
+            constexpr int kFull = BN / 32 * 32;  // columns read 32 at a time; the rest (16) at once
             float bv = -INFINITY;
             int bi = -1;
             float nan0 = 0.0f;
-            float v[32];
+            {
+                float v[32];
+                tc_ld32(taddr, v);
+                if (vt == 0 && v[0] != v[0]) nan0 = 1.0f;
+                scan_chunk<32>(v, 0, valid, bv, bi);
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                tc_ld32(taddr + uint32_t(c * 32), v);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = c * 32 + j;
-                    const float x = v[j];
-                    if (col < valid && (x > bv || (bi < 0 && x == x))) {
-                        bv = x;
-                        bi = col;
-                    }
+                for (int c = 32; c < kFull; c += 32) {
+                    tc_ld32(taddr + uint32_t(c), v);
+                    scan_chunk<32>(v, c, valid, bv, bi);
                 }
-                if (c == 0 && vt == 0 && v[0] != v[0]) nan0 = 1.0f;
+                if constexpr (BN % 32 != 0) {
+                    float w[16];
+                    tc_ld16(taddr + uint32_t(kFull), w);
+                    scan_chunk<16>(w, kFull, valid, bv, bi);
+                }
             }
             float sum = 0.0f;
             if (a.want_lse) {
                 // Every lane makes the same tcgen05.ld calls (they are warp-collective); a lane whose
                 // tile part is all NaN sums against 0 and discards the result.
-                const float l2e = 1.4426950408889634f;
-                const float mb = bi >= 0 ? bv * l2e : 0.0f;
+                const float mb = bi >= 0 ? bv * 1.4426950408889634f : 0.0f;
                 float s0 = 0.0f, s1 = 0.0f;
+                float v[32];
 #pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    tc_ld32(taddr + uint32_t(c * 32), v);
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const int col = c * 32 + j;
-                        if (col < valid) s0 += fast_exp2(__fsub_rn(__fmul_rn(v[j], l2e), mb));
-                        if (col + 1 < valid) s1 += fast_exp2(__fsub_rn(__fmul_rn(v[j + 1], l2e), mb));
-                    }
+                for (int c = 0; c < kFull; c += 32) {
+                    tc_ld32(taddr + uint32_t(c), v);
+                    sum_chunk<32>(v, c, valid, mb, s0, s1);
+                }
+                if constexpr (BN % 32 != 0) {
+                    float w[16];
+                    tc_ld16(taddr + uint32_t(kFull), w);
+                    sum_chunk<16>(w, kFull, valid, mb, s0, s1);
                 }
                 sum = bi >= 0 ? s0 + s1 : 0.0f;
             }
@@ -390,7 +452,43 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int64_t v_tiles_of(int64_t n_vocab) { return (n_vocab + kBN - 1) / kBN; }
+// The two tile widths: 256 ids, or 208 when that spreads the tiles over the SMs clearly more evenly
+// (151936 ids on one row tile: 594 tiles of 256 leave two SMs a fifth tile, 731 tiles of 208 fill 148
+// SMs five times within 1%). The workspace holds records for the narrower one.
+constexpr int kWideBN = 256, kNarrowBN = 208;
+
+int64_t v_tiles_of(int64_t n_vocab, int bn) { return (n_vocab + bn - 1) / bn; }
+
+int pick_bn(int64_t m_tiles, int64_t n_vocab, int sms) {
+    auto cost = [&](int bn) {
+        const int64_t tiles = m_tiles * v_tiles_of(n_vocab, bn);
+        return double((tiles + sms - 1) / sms) * bn;
+    };
+    return cost(kNarrowBN) < 0.97 * cost(kWideBN) ? kNarrowBN : kWideBN;
+}
+
+template <int BN>
+int launch_lm(const void* hidden, const void* weight, const LmArgs& a, int64_t hidden_dim, int sms,
+              cudaStream_t stream) {
+    using T = LmTile<BN>;
+    CUtensorMap map_h, map_w;
+    if (!make_map(&map_h, hidden, uint64_t(hidden_dim), uint64_t(a.rows), kBM) ||
+        !make_map(&map_w, weight, uint64_t(hidden_dim), uint64_t(a.n_vocab), BN))
+        return LOOM_SELECT_ECUDA;
+    static std::once_flag attr_once[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LOOM_SELECT_ECUDA;
+    cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once[dev], [&] {
+        attr_err = cudaFuncSetAttribute(lm_head_argmax_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(T::kSmemBytes));
+    });
+    if (attr_err != cudaSuccess) return LOOM_SELECT_ECUDA;
+    const int64_t tiles = int64_t(a.m_tiles) * a.v_tiles;
+    const int grid = int(tiles < sms ? tiles : sms);
+    lm_head_argmax_kernel<BN><<<grid, kThreads, T::kSmemBytes, stream>>>(map_h, map_w, a);
+    return cudaGetLastError() == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA;
+}
 
 }  // namespace
 }  // namespace loom_select
@@ -401,7 +499,7 @@ extern "C" {
 
 LOOM_SELECT_API size_t loom_lm_head_workspace_size(int64_t rows, int64_t n_vocab) {
     if (rows <= 0 || n_vocab <= 0) return 0;
-    return ws_layout(sizeof(float4), rows * v_tiles_of(n_vocab)).bytes;
+    return ws_layout(sizeof(float4), rows * v_tiles_of(n_vocab, kNarrowBN)).bytes;
 }
 
 LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, int64_t rows, int64_t hidden_dim,
@@ -414,45 +512,30 @@ LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, 
         return LOOM_SELECT_ESHAPE;
     if (reinterpret_cast<uintptr_t>(hidden) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
         return LOOM_SELECT_EINVAL;
-    const int64_t vt = v_tiles_of(n_vocab), mt = (rows + kBM - 1) / kBM;
-    if (mt * vt > (int64_t(1) << 31) - 1) return LOOM_SELECT_ESHAPE;
-    const WsLayout l = ws_layout(sizeof(float4), rows * vt);
+    const int64_t mt = (rows + kBM - 1) / kBM;
+    const int64_t vt_max = v_tiles_of(n_vocab, kNarrowBN);
+    if (mt * vt_max > (int64_t(1) << 31) - 1) return LOOM_SELECT_ESHAPE;
+    const WsLayout l = ws_layout(sizeof(float4), rows * vt_max);
     if (!workspace || workspace_bytes < l.bytes || reinterpret_cast<uintptr_t>(workspace) % kWsAlign != 0)
         return LOOM_SELECT_EWORKSPACE;
     int st = LOOM_SELECT_OK;
     const int sms = device_sm_count(&st);
     if (st != LOOM_SELECT_OK) return st;
 
-    CUtensorMap map_h, map_w;
-    if (!make_map(&map_h, hidden, uint64_t(hidden_dim), uint64_t(rows), kBM) ||
-        !make_map(&map_w, weight, uint64_t(hidden_dim), uint64_t(n_vocab), kBN))
-        return LOOM_SELECT_ECUDA;
-
-    static std::once_flag attr_once[64];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LOOM_SELECT_ECUDA;
-    cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once[dev], [&] {
-        attr_err = cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        int(kSmemBytes));
-    });
-    if (attr_err != cudaSuccess) return LOOM_SELECT_ECUDA;
-
+    const int bn = pick_bn(mt, n_vocab, sms);
     LmArgs a;
     a.rows = rows;
     a.n_vocab = n_vocab;
     a.k_blocks = int(hidden_dim / kBK);
     a.m_tiles = int(mt);
-    a.v_tiles = int(vt);
+    a.v_tiles = int(v_tiles_of(n_vocab, bn));
     a.records = reinterpret_cast<float4*>(static_cast<char*>(workspace) + l.records);
     a.status = static_cast<int*>(workspace);
     a.want_lse = out_lse != nullptr;
-    const int64_t tiles = mt * vt;
-    const int grid = int(tiles < sms ? tiles : sms);
     auto s = static_cast<cudaStream_t>(stream);
-    lm_head_argmax_kernel<<<grid, kThreads, kSmemBytes, s>>>(map_h, map_w, a);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return LOOM_SELECT_ECUDA;
+    st = bn == kNarrowBN ? launch_lm<kNarrowBN>(hidden, weight, a, hidden_dim, sms, s)
+                         : launch_lm<kWideBN>(hidden, weight, a, hidden_dim, sms, s);
+    if (st != LOOM_SELECT_OK) return st;
     lm_merge_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids,
                                                               out_logit, out_lse);
     return cudaGetLastError() == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA;
