@@ -42,20 +42,26 @@ constexpr int kBM = 128;          // rows per tile (MMA M)
 constexpr int kBK = 64;           // K slice per stage: 64 bf16 = 128 bytes, one swizzle span
 constexpr int kUK = 16;           // K per tcgen05.mma (kind::f16)
 constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
-constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kTmemCols = 512;              // two accumulators, 256 columns apart
 constexpr int kAccStride = 256;
 
 // A tile is kBM rows x BN ids; the ring holds as many K slices as fit in shared memory. BN is a
 // multiple of 16 (an MMA N for M = 128) and keeps every stage a multiple of 1024 bytes (the 128-byte
 // swizzle's repeat).
-template <int BN>
+template <int BN, bool kFewRows>
 struct LmTile {
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tile width");
+    // kFewRows (calls of at most 8 rows, i.e. decoding): the hidden tile is loaded 8 rows high
+    // (1 KiB) and the freed shared memory holds more weight stages in flight. The MMA still reads
+    // 128 rows of A; rows 8-127 are whatever follows in the stage and only reach TMEM lanes of rows
+    // that do not exist, whose results are never read.
+    static constexpr int kARows = kFewRows ? 8 : kBM;
+    static constexpr uint32_t kTileABytes = uint32_t(kARows) * kBK * 2;
     static constexpr uint32_t kTileBBytes = uint32_t(BN) * kBK * 2;
     static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
     static_assert(kStageBytes % 1024 == 0, "stage alignment");
-    static constexpr int kStages = int((227u * 1024u - 2048u) / kStageBytes) < 6 ? int((227u * 1024u - 2048u) / kStageBytes) : 6;
+    static constexpr int kStages = int((227u * 1024u - 2048u) / kStageBytes) < 8 ? int((227u * 1024u - 2048u) / kStageBytes) : 8;
+    static_assert(kStages >= 2 && kStageBytes >= kBM * kBK * 2, "the MMA's 128-row A read stays inside its stage");
     static constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 256 + 1024;  // ring + barriers + alignment
     // Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, N >> 3, M >> 4.
     static constexpr uint32_t kIdesc =
@@ -202,13 +208,14 @@ struct LmArgs {
     int want_lse;
 };
 
-template <int BN>
+template <int BN, bool kFewRows>
 __global__ void __launch_bounds__(kThreads, 1)
     lm_head_argmax_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                           const LmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using T = LmTile<BN>;
+    using T = LmTile<BN, kFewRows>;
+    constexpr uint32_t kTileABytes = T::kTileABytes;
     constexpr int kStages = T::kStages;
     constexpr uint32_t kStageBytes = T::kStageBytes;
     LmBars<kStages>* bars = reinterpret_cast<LmBars<kStages>*>(smem + size_t(kStages) * kStageBytes);
@@ -467,12 +474,12 @@ int pick_bn(int64_t m_tiles, int64_t n_vocab, int sms) {
     return cost(kNarrowBN) < 0.97 * cost(kWideBN) ? kNarrowBN : kWideBN;
 }
 
-template <int BN>
+template <int BN, bool kFewRows>
 int launch_lm(const void* hidden, const void* weight, const LmArgs& a, int64_t hidden_dim, int sms,
               cudaStream_t stream) {
-    using T = LmTile<BN>;
+    using T = LmTile<BN, kFewRows>;
     CUtensorMap map_h, map_w;
-    if (!make_map(&map_h, hidden, uint64_t(hidden_dim), uint64_t(a.rows), kBM) ||
+    if (!make_map(&map_h, hidden, uint64_t(hidden_dim), uint64_t(a.rows), uint32_t(T::kARows)) ||
         !make_map(&map_w, weight, uint64_t(hidden_dim), uint64_t(a.n_vocab), BN))
         return LOOM_SELECT_ECUDA;
     static std::once_flag attr_once[64];
@@ -480,13 +487,13 @@ int launch_lm(const void* hidden, const void* weight, const LmArgs& a, int64_t h
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LOOM_SELECT_ECUDA;
     cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once[dev], [&] {
-        attr_err = cudaFuncSetAttribute(lm_head_argmax_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err = cudaFuncSetAttribute(lm_head_argmax_kernel<BN, kFewRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(T::kSmemBytes));
     });
     if (attr_err != cudaSuccess) return LOOM_SELECT_ECUDA;
     const int64_t tiles = int64_t(a.m_tiles) * a.v_tiles;
     const int grid = int(tiles < sms ? tiles : sms);
-    lm_head_argmax_kernel<BN><<<grid, kThreads, T::kSmemBytes, stream>>>(map_h, map_w, a);
+    lm_head_argmax_kernel<BN, kFewRows><<<grid, kThreads, T::kSmemBytes, stream>>>(map_h, map_w, a);
     return cudaGetLastError() == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA;
 }
 
@@ -533,8 +540,13 @@ LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, 
     a.status = static_cast<int*>(workspace);
     a.want_lse = out_lse != nullptr;
     auto s = static_cast<cudaStream_t>(stream);
-    st = bn == kNarrowBN ? launch_lm<kNarrowBN>(hidden, weight, a, hidden_dim, sms, s)
-                         : launch_lm<kWideBN>(hidden, weight, a, hidden_dim, sms, s);
+    const bool few = rows <= 8;
+    if (bn == kNarrowBN)
+        st = few ? launch_lm<kNarrowBN, true>(hidden, weight, a, hidden_dim, sms, s)
+                 : launch_lm<kNarrowBN, false>(hidden, weight, a, hidden_dim, sms, s);
+    else
+        st = few ? launch_lm<kWideBN, true>(hidden, weight, a, hidden_dim, sms, s)
+                 : launch_lm<kWideBN, false>(hidden, weight, a, hidden_dim, sms, s);
     if (st != LOOM_SELECT_OK) return st;
     lm_merge_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids,
                                                               out_logit, out_lse);
