@@ -51,11 +51,11 @@ constexpr int kAccStride = 256;
 template <int BN, bool kFewRows>
 struct LmTile {
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tile width");
-    // kFewRows (calls of at most 8 rows, i.e. decoding): the hidden tile is loaded 8 rows high
-    // (1 KiB) and the freed shared memory holds more weight stages in flight. The MMA still reads
-    // 128 rows of A; rows 8-127 are whatever follows in the stage and only reach TMEM lanes of rows
+    // kFewRows (calls of at most 16 rows, i.e. decoding): the hidden tile is loaded 16 rows high
+    // (2 KiB) and the freed shared memory holds more weight stages in flight. The MMA still reads
+    // 128 rows of A; rows 16-127 are whatever follows in the stage and only reach TMEM lanes of rows
     // that do not exist, whose results are never read.
-    static constexpr int kARows = kFewRows ? 8 : kBM;
+    static constexpr int kARows = kFewRows ? 16 : kBM;
     static constexpr uint32_t kTileABytes = uint32_t(kARows) * kBK * 2;
     static constexpr uint32_t kTileBBytes = uint32_t(BN) * kBK * 2;
     static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
@@ -540,7 +540,7 @@ LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, 
     a.status = static_cast<int*>(workspace);
     a.want_lse = out_lse != nullptr;
     auto s = static_cast<cudaStream_t>(stream);
-    const bool few = rows <= 8;
+    const bool few = rows <= 16;
     if (bn == kNarrowBN)
         st = few ? launch_lm<kNarrowBN, true>(hidden, weight, a, hidden_dim, sms, s)
                  : launch_lm<kNarrowBN, false>(hidden, weight, a, hidden_dim, sms, s);

@@ -62,6 +62,8 @@ def _check(hidden, weight):
     (5, 1024, 1000),       # vocabulary not a multiple of the 256-id tile
     (200, 512, 4099),      # two row tiles, the second ragged; a 3-id last vocabulary tile
     (128, 64, 256),        # one K slice, exactly one tile
+    (16, 1024, 151936),    # the largest call that loads a 16-row hidden tile
+    (17, 512, 30011),      # the smallest that loads the full 128-row tile
     (1024, 2048, 151936),  # the 1024-row batch
 ])
 def test_lm_head_matches_fp32_reference(rows, hdim, vocab):
