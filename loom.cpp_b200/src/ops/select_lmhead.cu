@@ -14,8 +14,8 @@
 //   * warps 2-5 drain the other accumulator meanwhile (tcgen05.ld, one row per thread) and reduce each
 //     row's 256 logits to a record: the tile's maximum, the lowest id reaching it, the sum of
 //     exp(logit - maximum) when the log-sum-exp is wanted, and whether column 0 is NaN;
-//   * lm_merge_kernel folds a row's records (ascending id order) into the greedy id, its logit and
-//     the row's log-sum-exp.
+//   * lm_merge_kernel folds a row's records into the greedy id, its logit and the row's log-sum-exp
+//     (a warp per row, or the whole block per row for calls of at most 64 rows).
 //
 // Selection rule (generation.cpp:64-74, a strict '>' scan from id 0): the lowest id among equal
 // maxima wins, a NaN at id 0 wins, a NaN anywhere else never wins. The logits themselves are f32 sums
@@ -384,52 +384,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// One warp per row: the row's records in ascending id order fold into (id, logit, log-sum-exp).
+// A row's partial result: maximum, lowest id reaching it (-1: none, every logit NaN), and the sum of
+// exp(logit - maximum).
+struct LmPart {
+    float m;
+    int id;
+    float s;
+};
+
+// A partial sum moved to the maximum M (a part whose maximum is -inf adds nothing below a larger M).
+__device__ __forceinline__ float lm_rescale(const LmPart& p, float M) {
+    if (p.m == M) return p.s;
+    return p.m == -INFINITY ? 0.0f : p.s * expf(p.m - M);
+}
+
+// Folds two partial results of one row; the larger maximum wins, the lower id among equal maxima
+// (the strict '>' scan of generation.cpp:64-74 in any fold order), sums rescaled to the winner.
+__device__ __forceinline__ LmPart lm_fold(LmPart a, LmPart b) {
+    if (b.id < 0) return a;
+    if (a.id < 0) return b;
+    const bool take_b = b.m > a.m || (b.m == a.m && b.id < a.id);
+    LmPart r;
+    r.m = take_b ? b.m : a.m;
+    r.id = take_b ? b.id : a.id;
+    r.s = lm_rescale(a, r.m) + lm_rescale(b, r.m);
+    return r;
+}
+
+__device__ __forceinline__ LmPart lm_shfl_fold(LmPart p) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        LmPart q;
+        q.m = __shfl_xor_sync(0xffffffffu, p.m, o);
+        q.id = __shfl_xor_sync(0xffffffffu, p.id, o);
+        q.s = __shfl_xor_sync(0xffffffffu, p.s, o);
+        p = lm_fold(p, q);
+    }
+    return p;
+}
+
+// kTpr threads per row (32: a warp, 8 rows per block; 256: the whole block, for calls of few rows)
+// fold the row's tile records in one pass into (id, logit, log-sum-exp).
+template <int kTpr>
 __global__ void __launch_bounds__(256) lm_merge_kernel(const float4* __restrict__ records, int64_t rows, int v_tiles,
                                                        int want_lse, int32_t* __restrict__ out_ids,
                                                        float* __restrict__ out_logit, float* __restrict__ out_lse) {
-    const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
-    float bv = -INFINITY;
-    int bi = -1;
-    for (int t = lane; t < v_tiles; t += 32) {
-        const float4 rec = records[int64_t(t) * rows + r];
-        const int id = __float_as_int(rec.y);
-        if (id >= 0 && (bi < 0 || rec.x > bv)) {  // ascending tiles: strict '>' keeps the lowest id
-            bv = rec.x;
-            bi = id;
+    constexpr int kRowsPerBlock = 256 / kTpr;
+    const int64_t r = int64_t(blockIdx.x) * kRowsPerBlock + threadIdx.x / kTpr;
+    const int li = threadIdx.x % kTpr;
+    LmPart p{-INFINITY, -1, 0.0f};
+    if (r < rows) {
+        for (int t = li; t < v_tiles; t += kTpr) {
+            const float4 rec = records[int64_t(t) * rows + r];
+            const LmPart q{rec.x, __float_as_int(rec.y), rec.z};
+            p = lm_fold(p, q);
         }
     }
+    p = lm_shfl_fold(p);
+    if constexpr (kTpr == 256) {
+        __shared__ LmPart part[8];
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = p;
+        __syncthreads();
+        p = part[0];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
-            bv = ov;
-            bi = oi;
-        }
+        for (int w = 1; w < 8; ++w) p = lm_fold(p, part[w]);
     }
-    const float4 first = records[r];  // tile 0 carries the column-0 NaN flag
-    const bool nan0 = first.w != 0.0f;
-    float lse = 0.0f;
-    if (want_lse) {
-        float s = 0.0f;
-        if (bi >= 0) {
-            for (int t = lane; t < v_tiles; t += 32) {
-                const float4 rec = records[int64_t(t) * rows + r];
-                if (__float_as_int(rec.y) >= 0 && rec.x != -INFINITY) s += rec.z * expf(rec.x - bv);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        lse = (bi >= 0 && !nan0) ? bv + logf(s) : __int_as_float(0x7fc00000);
-    }
-    if (lane == 0) {
-        const bool zero = nan0 || bi < 0;  // a NaN at id 0 (or only NaNs) leaves the scan at id 0
-        out_ids[r] = zero ? 0 : bi;
-        if (out_logit) out_logit[r] = zero ? __int_as_float(0x7fc00000) : bv;
-        if (out_lse) out_lse[r] = lse;
+    if (li == 0 && r < rows) {
+        const bool nan0 = records[r].w != 0.0f;  // tile 0 carries the id-0 NaN flag
+        const bool zero = nan0 || p.id < 0;      // a NaN at id 0 (or only NaNs) leaves the scan at id 0
+        const float qnan = __int_as_float(0x7fc00000);
+        out_ids[r] = zero ? 0 : p.id;
+        if (out_logit) out_logit[r] = zero ? qnan : p.m;
+        if (out_lse && want_lse) out_lse[r] = zero ? qnan : p.m + logf(p.s);
     }
 }
 
@@ -548,8 +574,12 @@ LOOM_SELECT_API int loom_lm_head_argmax(const void* hidden, const void* weight, 
         st = few ? launch_lm<kWideBN, true>(hidden, weight, a, hidden_dim, sms, s)
                  : launch_lm<kWideBN, false>(hidden, weight, a, hidden_dim, sms, s);
     if (st != LOOM_SELECT_OK) return st;
-    lm_merge_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids,
-                                                              out_logit, out_lse);
+    if (rows <= 64)
+        lm_merge_kernel<256><<<unsigned(rows), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids, out_logit,
+                                                             out_lse);
+    else
+        lm_merge_kernel<32><<<unsigned((rows + 7) / 8), 256, 0, s>>>(a.records, rows, a.v_tiles, a.want_lse, out_ids,
+                                                                    out_logit, out_lse);
     return cudaGetLastError() == cudaSuccess ? LOOM_SELECT_OK : LOOM_SELECT_ECUDA;
 }
 
