@@ -243,5 +243,40 @@ inline SampleResult sample_rows(const float* d_logits, int64_t rows, int64_t n_v
     return r;
 }
 
+struct GreedyResult {
+    std::vector<int32_t> ids;    // per row: the greedy id
+    std::vector<float> logit;    // its logit
+    std::vector<float> logprob;  // its log-probability (logit - log-sum-exp of the row)
+};
+
+// The LM head's ggml_mul_mat(lm_head, hidden) followed by Generator::argmax
+// (src/core/generation.cpp:64-74), fused (loom_lm_head_argmax): d_hidden [rows, hidden_dim] and
+// d_weight [n_vocab, hidden_dim] are bf16 device arrays with packed rows; the logits are never
+// written. Results on the host.
+inline GreedyResult lm_head_argmax(const void* d_hidden, const void* d_weight, int64_t rows, int64_t hidden_dim,
+                                   int64_t n_vocab, cudaStream_t stream = nullptr) {
+    const size_t n = static_cast<size_t>(rows > 0 ? rows : 0);
+    const size_t col = detail::align256(n * sizeof(float));
+    detail::ThreadState& st = detail::state();
+    void* ws = st.workspace(loom_lm_head_workspace_size(rows, n_vocab), stream);
+    unsigned char* d = static_cast<unsigned char*>(st.device_out(3 * col + 1));
+    int32_t* ids = reinterpret_cast<int32_t*>(d);
+    float* logit = reinterpret_cast<float*>(d + col);
+    float* lse = reinterpret_cast<float*>(d + 2 * col);
+    detail::check(loom_lm_head_argmax(d_hidden, d_weight, rows, hidden_dim, n_vocab, ids, logit, lse, ws,
+                                      st.workspace_size(), stream),
+                  "lm_head_argmax");
+    const int status = loom_select_read_status(ws, stream);
+    if (status != LOOM_SELECT_OK) detail::check(status, "lm_head_argmax");
+    const unsigned char* h = static_cast<const unsigned char*>(detail::read_back(d, 3 * col, stream));
+    GreedyResult r;
+    r.ids.assign(reinterpret_cast<const int32_t*>(h), reinterpret_cast<const int32_t*>(h) + n);
+    r.logit.assign(reinterpret_cast<const float*>(h + col), reinterpret_cast<const float*>(h + col) + n);
+    const float* hl = reinterpret_cast<const float*>(h + 2 * col);
+    r.logprob.resize(n);
+    for (size_t i = 0; i < n; ++i) r.logprob[i] = r.logit[i] - hl[i];
+    return r;
+}
+
 }  // namespace select
 }  // namespace loom

@@ -8,6 +8,7 @@
 #include "loom_select.hpp"
 
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -115,6 +116,25 @@ static void gpu_checks() {
     CHECK_THROWS(sample_rows(ds, 2, 4, 4, db, 1, du, p), "outside the vocabulary");
     cudaFree(db);
     CHECK(r.probs.size() == 2 && r.probs[0] == 1.0f && r.probs[1] == 1.0f);
+
+    // the LM head fused with the greedy choice: hidden rows e0 and e1 (bf16), a [300, 64] weight that
+    // is zero except w[250][0] = 2, w[5][0] = 0.5, w[17][1] = 3 -> ids 250 and 17
+    std::vector<uint16_t> hid(2 * 64, 0), wt(300 * 64, 0);
+    hid[0] = 0x3F80;       // 1.0
+    hid[64 + 1] = 0x3F80;  // 1.0
+    wt[250 * 64 + 0] = 0x4000;  // 2.0
+    wt[5 * 64 + 0] = 0x3F00;    // 0.5
+    wt[17 * 64 + 1] = 0x4040;   // 3.0
+    uint16_t* dhid = upload(hid);
+    uint16_t* dwt = upload(wt);
+    const GreedyResult g = lm_head_argmax(dhid, dwt, 2, 64, 300);
+    CHECK((g.ids == std::vector<int32_t>{250, 17}));
+    CHECK(g.logit.size() == 2 && g.logit[0] == 2.0f && g.logit[1] == 3.0f);
+    const double lp0 = 2.0 - std::log(std::exp(2.0) + std::exp(0.5) + 298.0);
+    const double lp1 = 3.0 - std::log(std::exp(3.0) + 299.0);
+    CHECK(std::fabs(g.logprob[0] - lp0) < 1e-4 && std::fabs(g.logprob[1] - lp1) < 1e-4);
+    cudaFree(dhid);
+    cudaFree(dwt);
     for (void* p_ : {static_cast<void*>(d1), static_cast<void*>(d2), static_cast<void*>(d3), static_cast<void*>(da),
                      static_cast<void*>(dw), static_cast<void*>(ds), static_cast<void*>(du), static_cast<void*>(dh)})
         cudaFree(p_);
