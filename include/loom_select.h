@@ -18,6 +18,9 @@
  *                      no counterpart there and follows the semantics written beside it below.
  *   loom_sample_shard_partial / loom_sample_shard_merge
  *                      the same chain with the vocabulary split across GPUs; no counterpart.
+ *   loom_lm_head_argmax
+ *                      the text model's last ggml_mul_mat(lm_head, hidden) followed by
+ *                      Generator::argmax (src/core/generation.cpp:64-74), fused: the logits stay on chip.
  *
  * Conventions (those of loom.cpp's engine where it has one):
  *   - Every data pointer is DEVICE memory owned by the caller; the library keeps no pointer after a
@@ -101,7 +104,8 @@ LOOM_SELECT_API int loom_select_read_status(void* workspace, void* stream);
 
 /*
  * Test hook, no loom.cpp counterpart: drives the bounded-wait failure path of the streamed kernels
- * (argmax of long rows, the sampler for top_k <= 128) without any fault. It writes into the
+ * (argmax of long rows, the sampler for top_k <= 128) and of loom_lm_head_argmax (where the withheld
+ * stage is the first CTA's K slice number withhold_stage) without any fault. It writes into the
  * workspace header, on `stream`: wait_limit_ns (> 0) replaces the 2 s bound of every wait of those
  * kernels, and withhold_stage >= 0 makes the first CTA's producer leave that stage of its range
  * unissued, so its consumers' waits run out. The next such call records LOOM_SELECT_ETIMEOUT (its

@@ -185,13 +185,14 @@ __device__ __forceinline__ void sum_chunk(const float (&v)[W], int c0, int valid
 }
 
 // Bounded wait that also gives up as soon as another role of the CTA has aborted.
-__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag) {
+__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag,
+                                        uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit_ns) {
             record_status(status, LOOM_SELECT_ETIMEOUT);
             *abort_flag = 1;
             return false;
@@ -222,6 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The workspace header's test hook (zero for every normal caller): a lower wait bound, and one
+    // K slice that CTA 0's producer leaves unissued so that the MMA warp's wait runs out.
+    const WaitFault wf = read_wait_fault(a.status);
+    const uint64_t lim = wf.limit_ns;
     const int n_tiles = a.m_tiles * a.v_tiles;
 
     if (threadIdx.x == 0) {
@@ -252,16 +257,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // ---- producer: TMA into the ring ----
             int64_t kc = 0;
+            const int64_t withheld = (blockIdx.x == 0 && wf.withhold > 0) ? int64_t(wf.withhold) - 1 : -1;
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
                 const int mt = t % a.m_tiles, vt = t / a.m_tiles;
                 for (int kb = 0; kb < a.k_blocks; ++kb, ++kc) {
                     const int s = int(kc % kStages);
                     const int64_t n = kc / kStages;
-                    if (n >= 1 && !lm_wait(&bars->empty[s], uint32_t((n - 1) & 1), a.status, abort_flag)) {
+                    if (n >= 1 && !lm_wait(&bars->empty[s], uint32_t((n - 1) & 1), a.status, abort_flag, lim)) {
                         ok = false;
                         break;
                     }
+                    if (kc == withheld) continue;  // test hook only: this slice never arrives
                     unsigned char* st = smem + size_t(s) * kStageBytes;
                     mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
                     tma_load_2d(st, &map_h, kb * kBK, mt * kBM, &bars->full[s]);
@@ -270,10 +277,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Every copy issued lands before the CTA may exit (on the normal path the MMA warp has
             // consumed them all already and these waits return at once).
+            // (A withheld slice was the last use of its stage the producer reached: its next use
+            // waits for the MMA warp, which is stuck on the withheld one until the abort.)
             for (int s = 0; s < kStages; ++s) {
                 if (kc > s) {
-                    const int64_t last = (kc - 1 - s) / kStages;
-                    mbar_wait_bounded(&bars->full[s], uint32_t(last & 1), a.status);
+                    int64_t last_kc = s + int64_t(kStages) * ((kc - 1 - s) / kStages);
+                    if (last_kc == withheld) last_kc -= kStages;
+                    if (last_kc >= 0) mbar_wait_bounded(&bars->full[s], uint32_t((last_kc / kStages) & 1), a.status, lim);
                 }
             }
         }
@@ -286,13 +296,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++i) {
                 const int b = i & 1, u = i >> 1;
-                if (u >= 1 && !lm_wait(&bars->tempty[b], uint32_t((u - 1) & 1), a.status, abort_flag)) break;
+                if (u >= 1 && !lm_wait(&bars->tempty[b], uint32_t((u - 1) & 1), a.status, abort_flag, lim)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + uint32_t(b * kAccStride);
                 for (int kb = 0; kb < a.k_blocks; ++kb, ++kc) {
                     const int s = int(kc % kStages);
                     const int64_t n = kc / kStages;
-                    if (!lm_wait(&bars->full[s], uint32_t(n & 1), a.status, abort_flag)) {
+                    if (!lm_wait(&bars->full[s], uint32_t(n & 1), a.status, abort_flag, lim)) {
                         ok = false;
                         break;
                     }
@@ -310,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // All MMAs issued have completed before TMEM is freed.
             tc_commit(&bars->drain);
-            mbar_wait_bounded(&bars->drain, 0, a.status);
+            mbar_wait_bounded(&bars->drain, 0, a.status, lim);
         }
         __syncwarp();
     } else {
@@ -320,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int mt = t % a.m_tiles, vt = t / a.m_tiles;
             const int b = i & 1, u = i >> 1;
-            const bool ok = lm_wait(&bars->tfull[b], uint32_t(u & 1), a.status, abort_flag);
+            const bool ok = lm_wait(&bars->tfull[b], uint32_t(u & 1), a.status, abort_flag, lim);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * kAccStride);

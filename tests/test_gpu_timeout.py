@@ -74,3 +74,27 @@ def test_hook_rejects_bad_arguments(sel, dev):
     assert lib.loom_select_test_wait_fault(None, LIMIT_NS, 0, None) == sel.EWORKSPACE
     assert lib.loom_select_test_wait_fault(buf.data_ptr(), 0, 0, None) == sel.EINVAL
     assert lib.loom_select_test_wait_fault(buf.data_ptr(), LIMIT_NS, -2, None) == sel.EINVAL
+
+
+def test_lm_head_wait_runs_out_then_next_call_is_exact(sel, dev):
+    # the fused LM-head kernel: CTA 0's producer leaves its 4th K slice unissued, the MMA warp's wait
+    # runs out, every role winds down (copies and MMAs issued are drained, TMEM is freed)
+    g = torch.Generator(device="cuda").manual_seed(31)
+    h = torch.randn(64, 512, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(20000, 512, generator=g, device="cuda") / 22.6).to(torch.bfloat16)
+    ws = sel.Workspace(dev)
+    ids0, _, _ = sel.lm_head_argmax(h, w, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_status() == sel.OK
+    _arm(sel, ws, 3)
+    sel.lm_head_argmax(h, w, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_status() == sel.ETIMEOUT
+    _reset(sel, ws)
+    ids, logit, lse = sel.lm_head_argmax(h, w, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_status() == sel.OK
+    assert torch.equal(ids, ids0)
+    ref = h.float() @ w.float().t()
+    assert bool((ref.gather(1, ids.long()[:, None])[:, 0] >= ref.max(dim=1).values - 2e-3).all())
+    assert torch.allclose(lse, torch.logsumexp(ref, dim=1), atol=2e-3, rtol=0)
