@@ -660,7 +660,7 @@ def run_lm_head(args, sel, torch, dev, rank, world, peak):
     out = {"config": f"hidden [rows, {hdim}] bf16 x lm_head [{VOCAB}, {hdim}] bf16 (two alternating copies), "
                      "greedy id + logit + log-sum-exp per row",
            "tensor_peak_tflops": 1590.0, "tensor_peak_source": "fallback (no measured bf16 figure here)"}
-    for rows in (1, ROWS):
+    for rows in (1, 16, 128, ROWS):
         hidden = torch.randn(rows, hdim, generator=g, device=dev).to(torch.bfloat16)
         ids = torch.empty(rows, dtype=torch.int32, device=dev)
         logit = torch.empty(rows, dtype=torch.float32, device=dev)
