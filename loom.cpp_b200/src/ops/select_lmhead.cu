@@ -6,13 +6,14 @@
 // (src/core/generation.cpp:64-74) scans them. Here the product is computed tile by tile on the
 // tensor cores and reduced before it ever leaves the SM:
 //
-//   * one persistent CTA per SM walks 128-row x 256-id tiles (row tile fastest, so the CTAs running
-//     at the same time share one weight tile through L2 and the weight is read from HBM about once);
-//   * warp 0 streams 64-wide K slices of the hidden and weight tiles into a 4-stage shared-memory
-//     ring with TMA (128-byte swizzle); warp 1 issues tcgen05.mma (M 128, N 256, K 16, bf16 in,
-//     f32 accumulate) into one of two 256-column TMEM accumulators;
+//   * one persistent CTA per SM walks 128-row x BN-id tiles, BN 256 or 208 (row tile fastest, so the
+//     CTAs running at the same time share one weight tile through L2 and the weight is read from HBM
+//     about once);
+//   * warp 0 streams 64-wide K slices of the hidden and weight tiles into a shared-memory ring of 4-8
+//     stages with TMA (2-D tensor maps, 128-byte swizzle, no multicast); warp 1 issues tcgen05.mma
+//     (M 128, N BN, K 16, bf16 in, f32 accumulate) into one of two TMEM accumulators;
 //   * warps 2-5 drain the other accumulator meanwhile (tcgen05.ld, one row per thread) and reduce each
-//     row's 256 logits to a record: the tile's maximum, the lowest id reaching it, the sum of
+//     row's BN logits to a record: the tile's maximum, the lowest id reaching it, the sum of
 //     exp(logit - maximum) when the log-sum-exp is wanted, and whether column 0 is NaN;
 //   * lm_merge_kernel folds a row's records into the greedy id, its logit and the row's log-sum-exp
 //     (a warp per row, or the whole block per row for calls of at most 64 rows).
@@ -22,9 +23,10 @@
 // of exact bf16 products in the tensor cores' order, so they can differ from another GEMM's in the
 // last bits; the id is the exact argmax of the logits this kernel computes.
 //
-// Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records LOOM_SELECT_ETIMEOUT in
-// the workspace, raises the CTA's abort flag, and every role winds down: the producer waits (again
-// bounded) for the copies it issued, the MMA warp for the MMAs it issued, then TMEM is freed.
+// Every mbarrier wait is bounded (kWaitLimitNs, or the workspace test hook's lower bound). A wait
+// that runs out records LOOM_SELECT_ETIMEOUT in the workspace, raises the CTA's abort flag, and every
+// role winds down: the producer waits (again bounded) for the copies it issued, the MMA warp for the
+// MMAs it issued, then TMEM is freed.
 #include <cstdint>
 #include <cuda.h>
 #include <cudaTypedefs.h>
